@@ -1,0 +1,333 @@
+"""Benchmark: fused causal GQA prefill TFLOP/s at seq 8192 (+ decode HBM GB/s) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (one step = one launch of the fused kernel over one batch):
+  causal GQA prefill, Hq=32, Hkv=8, d=128, seq 8192, bf16, RoPE (theta 5e5) applied
+  in the kernel to the raw Q/K; Q,K ~ 2.5*N(0,1), V ~ N(0,1) (seeded synthetic).
+  N=1: batch 4 (the headline configuration).  N GPUs: batch 4N, rank r owns kv
+  heads [8r/N, 8(r+1)/N) of every sequence (KV-head sharding, no collective), so the
+  work per GPU is fixed ("weak" scaling).  Inputs (335 MB per rank) exceed L2.
+Also measured: split-KV decode, batch 64 (64N across ranks), cache lengths
+U[1024, 32768], reported in HBM GB/s under "decode".
+
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, S_PREFILL, B_PER_GPU = 32, 8, 128, 8192, 4
+DEC_B, DEC_LMAX = 64, 32768
+METRIC = "GQA causal prefill TFLOP/s (seq 8192) at 1/2/4/8 B200; decode HBM GB/s"
+
+
+def causal_flops(B, Hq, S, d):
+    return 4.0 * B * Hq * d * S * (S + 1) / 2.0
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p.get("bf16_tflops_sustained"), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def load_profile_traffic():
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, fl in rows for i, v in enumerate(fl) if v.lower().startswith("active")})
+        loaded = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_loop(fn, steps, world, stream):
+    """K back-to-back calls bracketed by barrier + synchronize; CUDA events on `stream`."""
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world)
+
+
+def cpu_reference_sample(heads: int, S: int, seed: int = 7):
+    """The reference's NumPy fp32 core (oracle port) on `heads` query heads of the
+    workload; returns (seconds, causal flops of the sample, threads)."""
+    from oracle import cpu_port
+    rng = np.random.default_rng(seed)
+    q = (rng.standard_normal((heads, S, D), dtype=np.float32) * np.float32(2.5))
+    k = (rng.standard_normal((1, S, D), dtype=np.float32) * np.float32(2.5))
+    v = rng.standard_normal((1, S, D), dtype=np.float32)
+    t0 = time.perf_counter()
+    for h in range(heads):
+        cpu_port.gqa_attention_head(q[h], k[0], v[0], causal=True)
+    dt = time.perf_counter() - t0
+    return dt, causal_flops(1, heads, S, D), os.cpu_count()
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    samples = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_reference_sample(1, S_PREFILL)
+        break
+    tot_t, tot_f = 0.0, 0.0
+    for _ in range(args.steps):
+        dt, fl, cores = cpu_reference_sample(1, S_PREFILL)
+        tot_t += dt
+        tot_f += fl
+        samples.append(dt)
+    val = tot_f / tot_t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot_t / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "gqa_causal_prefill", "sample": "1 query head (kv head 0) of batch element 0 per step",
+                   "seq_len": S_PREFILL, "q_heads": HQ, "kv_heads": HKV, "head_dim": D},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": "one (batch, q-head) of the seq-8192 workload per step; NumPy fp32 per-head "
+                                   "QK^T, triu mask, softmax, PV (CPU_Baseline gqa_attention_cpu restated)"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local):
+    from llama3_8b_attention_optimize_b200 import kernels
+    from llama3_8b_attention_optimize_b200.session import DecodeSession, PrefillSession
+    from llama3_8b_attention_optimize_b200.shard import kv_shard
+
+    sh = kv_shard(rank, world, HKV, HQ)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    B = B_PER_GPU * world  # global batch; this rank owns sh.kv_count kv heads of every sequence
+    hq, hkv = sh.q_count, sh.kv_count
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sess = PrefillSession(B, S_PREFILL, hq, hkv, D, causal=True, rope=True, device=dev)
+    sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev) * 2.5)
+    sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev) * 2.5)
+    sess.v.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
+
+    for _ in range(args.warmup):
+        sess.run_device()
+    kernels.device_check(dev)
+    flops_rank = causal_flops(B, hq, S_PREFILL, D)
+    with ClockSampler(local) as clk:
+        ms = time_loop(sess.run_device, args.steps, world, stream)
+    kernels.device_check(dev)
+    ms_step = ms / args.steps
+    flops_total = causal_flops(B, HQ, S_PREFILL, D)
+    value = flops_total / (ms_step * 1e-3) / 1e12
+
+    # ---- end to end through the host-buffer API (pinned host in, pinned host out)
+    qh = sess.q.to("cpu").pin_memory()
+    kh = sess.k.to("cpu").pin_memory()
+    vh = sess.v.to("cpu").pin_memory()
+    oh = torch.empty(sess.shape_q, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+    for _ in range(min(args.warmup, 2)):
+        sess.run_host(qh, kh, vh, oh)
+    ms_e2e = time_loop(lambda: sess.run_host(qh, kh, vh, oh), e2e_steps, world, stream) / e2e_steps
+    e2e_value = flops_total / (ms_e2e * 1e-3) / 1e12
+    del qh, kh, vh, oh
+
+    # ---- split-KV decode (HBM-bound), same sharding
+    dB = DEC_B * world
+    dgen = torch.Generator().manual_seed(99)
+    lens_all = torch.randint(1024, DEC_LMAX + 1, (dB,), generator=dgen, dtype=torch.int32)
+    ds = DecodeSession(dB, DEC_LMAX, hq, hkv, D, device=dev)
+    kc = torch.empty(dB, hkv, DEC_LMAX, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.empty_like(kc)
+    for b0 in range(0, dB, 8):
+        kc[b0:b0 + 8].normal_(generator=gen)
+        vc[b0:b0 + 8].normal_(generator=gen)
+    ds.q.copy_(torch.randn(ds.q.shape, generator=gen, device=dev))
+    ds.lens.copy_(lens_all.to(dev))
+    for _ in range(args.warmup):
+        ds.run_device(kc, vc)
+    kernels.device_check(dev)
+    dsteps = max(args.steps, 10)
+    ms_dec = time_loop(lambda: ds.run_device(kc, vc), dsteps, world, stream) / dsteps
+    kernels.device_check(dev)
+    dec_bytes_rank = float(lens_all.sum().item()) * hkv * D * 2 * 2
+    dec_bytes_total = float(lens_all.sum().item()) * HKV * D * 2 * 2
+    dec_gbs = dec_bytes_total / (ms_dec * 1e-3) / 1e9
+    del kc, vc
+
+    hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
+    prof = load_profile_traffic()
+    achieved = flops_rank / (ms_step * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": achieved / tc_peak, "peak_source": f"{peak_src} bf16 dense (burst)",
+            "traffic": prof.get("prefill_bytes_per_launch"),
+            "algorithmic_flops_per_launch": flops_rank}
+    dec_ach = dec_bytes_rank / (ms_dec * 1e-3) / 1e9
+    dec_roof = {"bound": "hbm", "achieved": dec_ach, "peak": hbm_peak, "unit": "GB/s", "frac": dec_ach / hbm_peak,
+                "traffic": prof.get("decode_bytes_per_launch"), "algorithmic_bytes_per_launch": dec_bytes_rank}
+
+    if rank != 0:
+        return 0
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        dt, fl, cores = cpu_reference_sample(2, S_PREFILL)
+        cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+               "sample": "2 query heads (kv head 0, batch element 0) of the seq-8192 workload, NumPy fp32 "
+                         "(CPU_Baseline gqa_attention_cpu restated), %.1f s" % dt}
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1); Q,K x2.5)",
+        "config": {"workload": "gqa_causal_prefill_fused_rope", "global_batch": B, "batch_per_gpu_equiv": B_PER_GPU,
+                   "seq_len": S_PREFILL, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "parallelism": f"kv_head_shard{world}", "l2": "inputs 335 MB/rank > L2 (126 MB)"},
+        "roofline": roof,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": sess.h2d_bytes() * world, "d2h_bytes_per_step": sess.d2h_bytes() * world,
+                "path": "PrefillSession.run_host: pinned host Q/K/V -> device -> gqa_prefill_bf16 -> pinned host O"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "decode": {"metric": "split-KV GQA decode HBM GB/s", "value": dec_gbs, "unit": "GB/s", "ms_per_step": ms_dec,
+                   "config": {"batch": dB, "max_len": DEC_LMAX, "lens": "U[1024,32768] seed 99",
+                              "kv_heads_per_gpu": hkv}, "roofline": dec_roof, "gpu_launches": 2 * dsteps},
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
+    world, rank, local = dist_setup(args)
+    try:
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

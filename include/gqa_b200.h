@@ -1,0 +1,133 @@
+/*
+ * gqa_b200.h -- C ABI of libgqa_b200.so, the sm_100a (B200) GQA attention core.
+ *
+ * The reference (xuanhaozhang883/Llama3-8B-Attention-Optimize) computes this path
+ * in Python: the bf16-staged golden model llama3_attention_golden_model.py and the
+ * fp32 NumPy CPU_Baseline.  Its only native interface is the HLS C++ mask kernel
+ *   extern "C" void attention_mask(const score_t raw[], score_t masked[],
+ *                                  int q_heads, int seq_len, bool causal,
+ *                                  score_t mask_value)
+ * (attention_mask_module/src/attention_mask.hpp:31-39).  Each entry point below
+ * names the reference function it replaces.
+ *
+ * Conventions for every entry point:
+ *  - All tensors are caller-owned DEVICE buffers of raw bf16 words (uint16),
+ *    contiguous, 16-byte aligned.  The library never allocates device memory.
+ *  - Layouts follow the golden model: per-head [head][token][dim]; a batch adds a
+ *    leading axis: Q/O [B][Hq][S][d], K/V [B][Hkv][S][d].  GQA maps query head h to
+ *    kv head h / (Hq/Hkv) by address (no KV duplication).
+ *  - Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream) and return a status: 0 = GQA_OK, negative = error (see gqa_strerror).
+ *    Arguments are validated on the host before any launch; nothing aborts.
+ *  - Kernels bound every internal wait; a wait that gives up records a sticky
+ *    device error that gqa_device_check() reports (GQA_ERR_DEVICE_TIMEOUT).
+ *  - Thread-safe; the only global state is per-device launch attributes.
+ */
+#ifndef GQA_B200_H_
+#define GQA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gqa_stream_t; /* == cudaStream_t */
+
+#define GQA_OK 0
+#define GQA_ERR_INVALID_ARGUMENT (-1) /* null pointer, bad size, bad flag */
+#define GQA_ERR_UNSUPPORTED (-2)      /* shape outside what the kernels implement */
+#define GQA_ERR_MISALIGNED (-3)       /* pointer not 16-byte aligned */
+#define GQA_ERR_CUDA (-4)             /* CUDA runtime / driver error at launch */
+#define GQA_ERR_DEVICE_TIMEOUT (-5)   /* a kernel's bounded wait expired */
+#define GQA_ERR_WORKSPACE (-6)        /* workspace missing or too small */
+#define GQA_ERR_NO_DEVICE (-7)        /* no usable sm_100 device */
+
+#define GQA_FLAG_CAUSAL 1 /* mask keys j > i (golden :180-181) */
+#define GQA_FLAG_ROPE_Q 2 /* rotate Q in the kernel (golden apply_rope :162-163) */
+#define GQA_FLAG_ROPE_K 4 /* rotate K in the kernel (golden apply_rope :164) */
+
+#define GQA_MASK_NEG_INF_BF16 0xFF80 /* attention_mask.hpp:16 */
+
+/* Human-readable text for a status code. */
+const char* gqa_strerror(int code);
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int gqa_version(void);
+
+/* Synchronize `stream`, then report (and clear) the sticky device error:
+ * GQA_OK, GQA_ERR_DEVICE_TIMEOUT (site code in *site if non-NULL) or GQA_ERR_CUDA. */
+int gqa_device_check(gqa_stream_t stream, int* site);
+
+/* ---------------------------------------------------------------- RoPE
+ * Replaces build_rope_cache (llama3_attention_golden_model.py:124-130):
+ * cos/sin [seq_len][head_dim] bf16 for positions pos0..pos0+seq_len-1 with
+ * emb = cat(freqs, freqs), freqs = fp32(pos * fp32(1/theta^(2i/d))).          */
+int gqa_rope_cache_bf16(void* cos, void* sin, int seq_len, int head_dim, int pos0, double theta,
+                        gqa_stream_t stream);
+
+/* Replaces rotate_half/apply_rope (:133-139, used :162-164):
+ * y = bf16(x*cos + rotate_half(x)*sin), x/y [num_heads][seq_len][head_dim]
+ * (num_heads = B*H for batched buffers), table rows pos0..pos0+seq_len-1.
+ * y may alias x.                                                               */
+int gqa_rope_bf16(const void* x, void* y, const void* cos, const void* sin, int num_heads, int seq_len, int head_dim,
+                  int pos0, gqa_stream_t stream);
+
+/* ---------------------------------------------------------------- debug stages
+ * Per-stage kernels of the golden model's dump mode (:157-190); each is
+ * bit-exact with the golden's bf16 boundary rounding.                          */
+
+/* scores_before_mask (:175-176): bf16(fp32(q.k) * scale), [B][Hq][S][S]. */
+int gqa_scores_bf16(const void* q, const void* k, void* scores, int B, int Hq, int Hkv, int seq_len, int head_dim,
+                    float scale, gqa_stream_t stream);
+
+/* scores_after_mask (:180-181): bf16(score + (j > i ? -inf : +0)), [rows=B*Hq][S][S]. */
+int gqa_mask_bf16(const void* scores, void* masked, int num_heads, int seq_len, int causal, gqa_stream_t stream);
+
+/* Replaces the HLS kernel attention_mask (attention_mask.cpp:3-58): raw 16-bit
+ * word pass-through, `mask_value` where causal && k_token > q_token.  Unlike the
+ * HLS kernel (which returns silently), invalid sizes return an error.          */
+int gqa_attention_mask_bf16(const void* raw_scores, void* masked_scores, int q_heads, int seq_len, int causal,
+                            uint16_t mask_value, gqa_stream_t stream);
+
+/* softmax_weights (:185): bf16(softmax(x)) over the last axis of [rows][cols]. */
+int gqa_softmax_bf16(const void* scores, void* probs, long long rows, int cols, gqa_stream_t stream);
+
+/* attn_out_per_head (:189): bf16(sum_j fp32 p*v), p [B][Hq][S][S], v [B][Hkv][S][d]. */
+int gqa_pv_bf16(const void* probs, const void* v, void* out, int B, int Hq, int Hkv, int seq_len, int head_dim,
+                gqa_stream_t stream);
+
+/* ---------------------------------------------------------------- fused prefill
+ * Replaces the core of run_full_attention (:162-190) and gqa_attention_cpu
+ * (CPU_Baseline/cpu_baseline/attention.py:60-84) in one tcgen05 kernel:
+ *   O = softmax(mask(rope(Q) rope(K)^T * scale)) V, bf16 out [B][Hq][S][d].
+ * Processes kv heads [kv_head_begin, kv_head_begin+kv_head_count) of buffers
+ * holding Hq / Hkv heads (the KV-head shard of one GPU).  Requires head_dim=128,
+ * Hq = 4*Hkv.  cos/sin [>= S][128] (from gqa_rope_cache_bf16) are read when
+ * GQA_FLAG_ROPE_Q / GQA_FLAG_ROPE_K are set; Q/K buffers are never modified.    */
+int gqa_prefill_bf16(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B,
+                     int seq_len, int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, float scale,
+                     int flags, gqa_stream_t stream);
+
+/* ---------------------------------------------------------------- split-KV decode
+ * One query token per sequence against a KV cache (no reference function; the
+ * single-row case of attention.py:60-84).  q/o [B][Hq][d]; kcache/vcache
+ * [B][Hkv][max_len][d] (RoPE already applied); lens [B] int32 on the device:
+ * sequence b attends keys [0, lens[b]) (lens clamped to [0, max_len]).  With
+ * GQA_FLAG_ROPE_Q, q is rotated at position q_pos[b] (device int32 [B], clamped to
+ * [0, max_len]) using cos/sin tables of at least max_len+1 rows.  Work is split along the
+ * keys into chunks of `split_len` keys (multiple of 64, 0 = automatic); partial
+ * results go to `workspace` (gqa_decode_workspace_size bytes) and a log-sum-exp
+ * combine writes o.                                                            */
+size_t gqa_decode_workspace_size(int B, int Hq, int max_len, int split_len);
+int gqa_decode_bf16(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
+                    const void* cos, const void* sin, void* o, void* workspace, size_t workspace_bytes, int B,
+                    int max_len, int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
+                    float scale, int flags, gqa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GQA_B200_H_ */

@@ -1,0 +1,80 @@
+// capi.cu -- C-ABI glue: status strings, device-error readback, TMA descriptor
+// encoding, and the extern "C" entry of the fused prefill kernel.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "gqa_internal.h"
+
+namespace gqa {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void resolve_encode() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+
+}  // namespace
+
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long dim0, long long dim1, long long dim2, int box0,
+                      int box1, int box2) {
+  std::call_once(g_encode_once, resolve_encode);
+  if (!g_encode) return GQA_ERR_NO_DEVICE;
+  if (box0 * 2 > 128 || box0 <= 0 || box1 <= 0 || box2 <= 0 || box1 > 256 || box2 > 256) return GQA_ERR_UNSUPPORTED;
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(dim0), static_cast<cuuint64_t>(dim1), static_cast<cuuint64_t>(dim2)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(dim0) * 2, static_cast<cuuint64_t>(dim0 * dim1) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), static_cast<cuuint32_t>(box2)};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_UNSUPPORTED;
+}
+
+}  // namespace gqa
+
+using namespace gqa;
+
+extern "C" const char* gqa_strerror(int code) {
+  switch (code) {
+    case GQA_OK: return "ok";
+    case GQA_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, size or flag)";
+    case GQA_ERR_UNSUPPORTED: return "unsupported shape (head_dim must be 128 and Hq = 4*Hkv)";
+    case GQA_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+    case GQA_ERR_CUDA: return "CUDA error";
+    case GQA_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired (device error flag set)";
+    case GQA_ERR_WORKSPACE: return "workspace missing or too small";
+    case GQA_ERR_NO_DEVICE: return "no usable sm_100 device / driver entry point";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int gqa_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
+  if (site) *site = 0;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return GQA_ERR_CUDA;
+  int flag = 0;
+  if (cudaMemcpyFromSymbol(&flag, g_gqa_dev_error, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (flag == 0) return GQA_OK;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_gqa_dev_error, &zero, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (site) *site = flag;
+  return GQA_ERR_DEVICE_TIMEOUT;
+}
+
+extern "C" int gqa_prefill_bf16(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin,
+                                int B, int seq_len, int Hq, int Hkv, int head_dim, int kv_head_begin,
+                                int kv_head_count, float scale, int flags, gqa_stream_t stream) {
+  return launch_prefill(q, k, v, o, cos, sin, B, seq_len, Hq, Hkv, head_dim, kv_head_begin, kv_head_count, scale,
+                        flags, stream);
+}

@@ -1,0 +1,38 @@
+// gqa_internal.h -- host-side helpers shared by the kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "../../include/gqa_b200.h"
+
+namespace gqa {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Encode a 3-D bf16 tensor map over a contiguous [dim2][dim1][dim0] array with a
+// (box0, box1, box2) box and 128-byte swizzle (box0 * 2 bytes must be <= 128).
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long dim0, long long dim1, long long dim2, int box0,
+                      int box1, int box2);
+
+// Set cudaFuncAttributeMaxDynamicSharedMemorySize once per device for `func`.
+template <typename F>
+int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_NO_DEVICE;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done_mask.load(std::memory_order_acquire) & bit) return GQA_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return GQA_ERR_CUDA;
+  done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return GQA_OK;
+}
+
+int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
+                   int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
+                   cudaStream_t stream);
+
+}  // namespace gqa

@@ -1,0 +1,232 @@
+"""Torch-facing wrappers over the C ABI (one function per entry point).
+
+All tensors are CUDA bf16, contiguous; calls are enqueued on the current torch
+stream.  Shapes follow the reference's golden model: per-head [H][S][d], with an
+optional leading batch axis.  Raises ``GqaError`` on any non-zero status.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import GQA_FLAG_CAUSAL, GQA_FLAG_ROPE_K, GQA_FLAG_ROPE_Q, GqaError, check
+
+ROPE_THETA = 500000.0
+HEAD_DIM = 128
+
+
+def default_scale(head_dim: int = HEAD_DIM) -> float:
+    """fl32(1/sqrt(d)), the golden's ``scale`` (llama3_attention_golden_model.py:175)."""
+    return float(torch.tensor(1.0 / math.sqrt(head_dim), dtype=torch.float32))
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _need(t: torch.Tensor, name: str, dtype=torch.bfloat16) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the kernels have no CPU path)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def rope_cache(seq_len: int, head_dim: int = HEAD_DIM, theta: float = ROPE_THETA, pos0: int = 0,
+               device=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cos, sin) bf16 [seq_len][head_dim] on the device (golden build_rope_cache :124-130)."""
+    device = torch.device(device or "cuda")
+    cos = torch.empty(seq_len, head_dim, dtype=torch.bfloat16, device=device)
+    sin = torch.empty_like(cos)
+    check(_lib.load().gqa_rope_cache_bf16(_ptr(cos), _ptr(sin), seq_len, head_dim, pos0, float(theta),
+                                          _stream(device)), "gqa_rope_cache_bf16")
+    return cos, sin
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, pos0: int = 0,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(x*cos + rotate_half(x)*sin) for x [..., S, d] (golden apply_rope :133-139)."""
+    _need(x, "x")
+    _need(cos, "cos")
+    _need(sin, "sin")
+    S, d = x.shape[-2], x.shape[-1]
+    if cos.shape[-1] != d or cos.shape[0] < pos0 + S:
+        raise ValueError("rope table too short or wrong width")
+    out = torch.empty_like(x) if out is None else out
+    _need(out, "out")
+    heads = x.numel() // (S * d)
+    check(_lib.load().gqa_rope_bf16(_ptr(x), _ptr(out), _ptr(cos), _ptr(sin), heads, S, d, pos0, _stream(x.device)),
+          "gqa_rope_bf16")
+    return out
+
+
+def _bhsd(x: torch.Tensor, name: str) -> torch.Tensor:
+    if x.dim() == 3:
+        return x.unsqueeze(0)
+    if x.dim() != 4:
+        raise ValueError(f"{name} must be [H,S,d] or [B,H,S,d]")
+    return x
+
+
+def scores(q: torch.Tensor, k: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+    """bf16(q k^T * scale) [B,Hq,S,S] (golden scores_before_mask :175-176)."""
+    _need(q, "q")
+    _need(k, "k")
+    q4, k4 = _bhsd(q, "q"), _bhsd(k, "k")
+    B, Hq, S, d = q4.shape
+    Hkv = k4.shape[1]
+    out = torch.empty(B, Hq, S, S, dtype=torch.bfloat16, device=q.device)
+    check(_lib.load().gqa_scores_bf16(_ptr(q4), _ptr(k4), _ptr(out), B, Hq, Hkv, S, d,
+                                      default_scale(d) if scale is None else float(scale), _stream(q.device)),
+          "gqa_scores_bf16")
+    return out if q.dim() == 4 else out[0]
+
+
+def mask(s: torch.Tensor, causal: bool = True) -> torch.Tensor:
+    """bf16(s + triu(-inf, 1)) (golden scores_after_mask :180-181)."""
+    _need(s, "scores")
+    S = s.shape[-1]
+    out = torch.empty_like(s)
+    check(_lib.load().gqa_mask_bf16(_ptr(s), _ptr(out), s.numel() // (S * S), S, int(causal), _stream(s.device)),
+          "gqa_mask_bf16")
+    return out
+
+
+def attention_mask_words(raw: torch.Tensor, q_heads: int, seq_len: int, causal: bool = True,
+                         mask_value: int = _lib.GQA_MASK_NEG_INF_BF16) -> torch.Tensor:
+    """Raw-word mask of the HLS kernel (attention_mask.cpp:3-58) on int16/bf16 words."""
+    if raw.dtype not in (torch.int16, torch.bfloat16, torch.uint16):
+        raise TypeError("raw must hold 16-bit words")
+    if not raw.is_cuda or not raw.is_contiguous():
+        raise ValueError("raw must be a contiguous CUDA tensor")
+    out = torch.empty_like(raw)
+    check(_lib.load().gqa_attention_mask_bf16(_ptr(raw), _ptr(out), q_heads, seq_len, int(causal), mask_value,
+                                              _stream(raw.device)), "gqa_attention_mask_bf16")
+    return out
+
+
+def softmax(s: torch.Tensor) -> torch.Tensor:
+    """bf16(softmax(s, -1)) (golden softmax_weights :185)."""
+    _need(s, "scores")
+    out = torch.empty_like(s)
+    cols = s.shape[-1]
+    check(_lib.load().gqa_softmax_bf16(_ptr(s), _ptr(out), s.numel() // cols, cols, _stream(s.device)),
+          "gqa_softmax_bf16")
+    return out
+
+
+def pv(p: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """bf16(p v) with fp32 accumulation (golden attn_out_per_head :189)."""
+    _need(p, "probs")
+    _need(v, "v")
+    p4, v4 = _bhsd(p, "p"), _bhsd(v, "v")
+    B, Hq, S, _ = p4.shape
+    Hkv, d = v4.shape[1], v4.shape[3]
+    out = torch.empty(B, Hq, S, d, dtype=torch.bfloat16, device=p.device)
+    check(_lib.load().gqa_pv_bf16(_ptr(p4), _ptr(v4), _ptr(out), B, Hq, Hkv, S, d, _stream(p.device)), "gqa_pv_bf16")
+    return out if p.dim() == 4 else out[0]
+
+
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor | None = None,
+            sin: torch.Tensor | None = None, *, causal: bool = True, rope_q: bool = False, rope_k: bool = False,
+            scale: float | None = None, kv_heads: tuple[int, int] | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused GQA attention core (tcgen05): O = softmax(mask(rope(Q) rope(K)^T * scale)) V.
+
+    q [B,Hq,S,128], k/v [B,Hkv,S,128] (or without B); rope_q/rope_k rotate in the
+    kernel with the (cos, sin) tables of ``rope_cache``.  ``kv_heads=(begin, count)``
+    restricts the work to one KV-head shard; other heads of ``out`` are untouched.
+    """
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, n)
+    q4, k4, v4 = _bhsd(q, "q"), _bhsd(k, "k"), _bhsd(v, "v")
+    B, Hq, S, d = q4.shape
+    Hkv = k4.shape[1]
+    if k4.shape != (B, Hkv, S, d) or v4.shape != k4.shape:
+        raise ValueError("k and v must be [B,Hkv,S,d] matching q")
+    flags = (GQA_FLAG_CAUSAL if causal else 0) | (GQA_FLAG_ROPE_Q if rope_q else 0) | (GQA_FLAG_ROPE_K if rope_k else 0)
+    if (rope_q or rope_k):
+        if cos is None or sin is None:
+            raise ValueError("rope_q/rope_k need cos and sin tables")
+        _need(cos, "cos")
+        _need(sin, "sin")
+        if cos.shape[0] < S or cos.shape[1] != d:
+            raise ValueError("rope table shorter than the sequence")
+    if out is None:
+        out = torch.empty_like(q4)
+    _need(out, "out")
+    kb, kc = (0, Hkv) if kv_heads is None else kv_heads
+    check(_lib.load().gqa_prefill_bf16(_ptr(q4), _ptr(k4), _ptr(v4), _ptr(out),
+                                       _ptr(cos) if cos is not None else None, _ptr(sin) if sin is not None else None,
+                                       B, S, Hq, Hkv, d, kb, kc, default_scale(d) if scale is None else float(scale),
+                                       flags, _stream(q.device)), "gqa_prefill_bf16")
+    return out if q.dim() == 4 else out[0]
+
+
+def decode_workspace_bytes(B: int, Hq: int, max_len: int, split_len: int = 0) -> int:
+    return int(_lib.load().gqa_decode_workspace_size(B, Hq, max_len, split_len))
+
+
+def decode(q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, lens: torch.Tensor, *,
+           q_pos: torch.Tensor | None = None, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+           workspace: torch.Tensor | None = None, split_len: int = 0, scale: float | None = None,
+           kv_heads: tuple[int, int] | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Split-KV decode: q [B,Hq,128] against kcache/vcache [B,Hkv,Lmax,128]; lens int32 [B].
+
+    With ``q_pos`` (int32 [B]) and (cos, sin), q is rotated at q_pos[b] in the kernel.
+    """
+    for t, n in ((q, "q"), (kcache, "kcache"), (vcache, "vcache")):
+        _need(t, n)
+    _need(lens, "lens", torch.int32)
+    B, Hq, d = q.shape
+    Hkv, Lmax = kcache.shape[1], kcache.shape[2]
+    if kcache.shape != (B, Hkv, Lmax, d) or vcache.shape != kcache.shape or lens.shape != (B,):
+        raise ValueError("bad decode shapes")
+    flags = 0
+    if q_pos is not None:
+        _need(q_pos, "q_pos", torch.int32)
+        _need(cos, "cos")
+        _need(sin, "sin")
+        if cos.shape[0] < Lmax + 1 or sin.shape[0] < Lmax + 1:
+            raise ValueError("decode rope tables need max_len + 1 rows")
+        flags |= GQA_FLAG_ROPE_Q
+    need = decode_workspace_bytes(B, Hq, Lmax, split_len)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q) if out is None else out
+    kb, kc = (0, Hkv) if kv_heads is None else kv_heads
+    check(_lib.load().gqa_decode_bf16(_ptr(q), _ptr(kcache), _ptr(vcache), _ptr(lens),
+                                      _ptr(q_pos) if q_pos is not None else None,
+                                      _ptr(cos) if cos is not None else None, _ptr(sin) if sin is not None else None,
+                                      _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                      B, Lmax, Hq, Hkv, d, kb, kc, split_len,
+                                      default_scale(d) if scale is None else float(scale), flags, _stream(q.device)),
+          "gqa_decode_bf16")
+    return out
+
+
+def device_check(device=None) -> None:
+    """Synchronize and raise if any kernel's bounded wait expired since the last check."""
+    device = torch.device(device or "cuda")
+    site = ctypes_int()
+    rc = _lib.load().gqa_device_check(_stream(device), site)
+    if rc != 0:
+        raise GqaError(rc, f"device check (site 0x{site.value:x})")
+
+
+def ctypes_int():
+    import ctypes
+    return ctypes.c_int(0)
+
+
+__all__ = ["rope_cache", "rope", "scores", "mask", "attention_mask_words", "softmax", "pv", "prefill", "decode",
+           "decode_workspace_bytes", "device_check", "default_scale", "GqaError"]

@@ -1,0 +1,73 @@
+"""Host-buffer entry points: the call a user makes with Q/K/V in (pinned) host memory.
+
+``PrefillSession`` / ``DecodeSession`` own the device buffers and RoPE tables for
+one shape, so repeated calls allocate nothing; each call copies the inputs
+host->device, runs the kernel and copies the result device->host on the
+current stream.  This is the end-to-end path that replaces calling the
+reference's ``gqa_attention_cpu`` / ``run_full_attention`` on host arrays.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+
+
+class PrefillSession:
+    def __init__(self, B: int, S: int, Hq: int, Hkv: int, head_dim: int = 128, *, causal: bool = True,
+                 rope: bool = True, theta: float = kernels.ROPE_THETA, device=None):
+        self.device = torch.device(device or "cuda")
+        self.shape_q = (B, Hq, S, head_dim)
+        self.shape_kv = (B, Hkv, S, head_dim)
+        mk = lambda shp: torch.empty(shp, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        self.q, self.k, self.v, self.o = mk(self.shape_q), mk(self.shape_kv), mk(self.shape_kv), mk(self.shape_q)
+        self.causal, self.rope = causal, rope
+        self.cos, self.sin = kernels.rope_cache(S, head_dim, theta, device=self.device) if rope else (None, None)
+
+    def h2d_bytes(self) -> int:
+        return (self.q.numel() + self.k.numel() + self.v.numel()) * 2
+
+    def d2h_bytes(self) -> int:
+        return self.o.numel() * 2
+
+    def run_device(self) -> torch.Tensor:
+        return kernels.prefill(self.q, self.k, self.v, self.cos, self.sin, causal=self.causal, rope_q=self.rope,
+                               rope_k=self.rope, out=self.o)
+
+    def run_host(self, q_h: torch.Tensor, k_h: torch.Tensor, v_h: torch.Tensor, out_h: torch.Tensor) -> torch.Tensor:
+        """q_h/k_h/v_h/out_h: bf16 CPU tensors (pin them for asynchronous copies)."""
+        self.q.copy_(q_h, non_blocking=True)
+        self.k.copy_(k_h, non_blocking=True)
+        self.v.copy_(v_h, non_blocking=True)
+        self.run_device()
+        out_h.copy_(self.o, non_blocking=True)
+        return out_h
+
+
+class DecodeSession:
+    def __init__(self, B: int, Lmax: int, Hq: int, Hkv: int, head_dim: int = 128, *, split_len: int = 0,
+                 rope_q: bool = True, theta: float = kernels.ROPE_THETA, device=None):
+        self.device = torch.device(device or "cuda")
+        self.B, self.Lmax, self.Hq, self.Hkv = B, Lmax, Hq, Hkv
+        self.split_len = split_len
+        self.q = torch.empty(B, Hq, head_dim, dtype=torch.bfloat16, device=self.device)
+        self.o = torch.empty_like(self.q)
+        self.lens = torch.empty(B, dtype=torch.int32, device=self.device)
+        self.ws = torch.empty(kernels.decode_workspace_bytes(B, Hq, Lmax, split_len), dtype=torch.uint8,
+                              device=self.device)
+        self.cos, self.sin = kernels.rope_cache(Lmax + 1, head_dim, theta, device=self.device) if rope_q else (None, None)
+        self.rope_q = rope_q
+
+    def run_device(self, kcache: torch.Tensor, vcache: torch.Tensor) -> torch.Tensor:
+        return kernels.decode(self.q, kcache, vcache, self.lens, q_pos=self.lens if self.rope_q else None,
+                              cos=self.cos, sin=self.sin, workspace=self.ws, split_len=self.split_len, out=self.o)
+
+    def run_host(self, q_h: torch.Tensor, lens_h: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+                 out_h: torch.Tensor) -> torch.Tensor:
+        """One decode step: the new tokens' q and the cache lengths come from the host;
+        the KV cache stays resident on the device (as in serving)."""
+        self.q.copy_(q_h, non_blocking=True)
+        self.lens.copy_(lens_h, non_blocking=True)
+        self.run_device(kcache, vcache)
+        out_h.copy_(self.o, non_blocking=True)
+        return out_h

@@ -1,0 +1,47 @@
+"""Shared helpers for the test suite (seeded inputs, bf16 word views, ulp metrics)."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import golden as g
+
+
+def bf16_words(t: torch.Tensor) -> np.ndarray:
+    """bf16 tensor (any device) -> uint16 numpy words."""
+    return t.detach().to("cpu").contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def words_to_bf16(w: np.ndarray, device="cuda") -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(w, np.uint16).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def randn_bf16(shape, seed: int, scale: float = 1.0, device="cuda") -> torch.Tensor:
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=gen, dtype=torch.float32) * scale
+    return x.to(torch.bfloat16).to(device)
+
+
+def ulp_dist(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    def key(w):
+        w = w.astype(np.int64)
+        return np.where(w & 0x8000, 0x8000 - (w & 0x7FFF), 0x8000 + w)
+    return np.abs(key(a) - key(b))
+
+
+def ulp_histogram(a_words: np.ndarray, b_words: np.ndarray) -> dict:
+    d = ulp_dist(a_words, b_words)
+    return {"0": float((d == 0).mean()), "1": float((d == 1).mean()), "2": float((d == 2).mean()),
+            ">2": float((d > 2).mean()), "max": int(d.max()) if d.size else 0}
+
+
+def rows_reference(q_rot_w, k_rot_w, v_w, heads, pos, causal=True, n_keys=None) -> np.ndarray:
+    """Exact float64-accumulated attention rows from the oracle (per batch element)."""
+    return g.attention_rows(q_rot_w, k_rot_w, v_w, heads, pos, causal=causal, n_keys=n_keys)
+
+
+def bf16_ulp_of(x: np.ndarray) -> np.ndarray:
+    """Size of one bf16 ulp at |x| (for the output-rounding allowance)."""
+    ax = np.maximum(np.abs(x).astype(np.float32), np.float32(2.0 ** -126))
+    e = np.floor(np.log2(ax))
+    return np.exp2(e - 7).astype(np.float32)
