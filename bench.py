@@ -306,8 +306,40 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+def run_profile_case(args):
+    """Small cases for ncu captures (inputs > L2, a few hundred MB on the device):
+    prefill: B=2, seq 8192, 32/8 heads, fused RoPE; decode: B=8, cache 32768 keys."""
+    from llama3_8b_attention_optimize_b200 import kernels
+    from llama3_8b_attention_optimize_b200.session import DecodeSession, PrefillSession
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    if args.profile_case == "prefill":
+        sess = PrefillSession(2, S_PREFILL, HQ, HKV, D, device=dev)
+        sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev) * 2.5)
+        sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev) * 2.5)
+        sess.v.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
+        fn = sess.run_device
+    else:
+        B = 8
+        ds = DecodeSession(B, DEC_LMAX, HQ, HKV, D, device=dev)
+        kc = torch.randn(B, HKV, DEC_LMAX, D, generator=gen, device=dev).to(torch.bfloat16)
+        vc = torch.randn(B, HKV, DEC_LMAX, D, generator=gen, device=dev).to(torch.bfloat16)
+        ds.q.copy_(torch.randn(ds.q.shape, generator=gen, device=dev))
+        ds.lens.copy_(torch.randint(1024, DEC_LMAX + 1, (B,), generator=torch.Generator().manual_seed(99),
+                                    dtype=torch.int32).to(dev))
+        fn = lambda: ds.run_device(kc, vc)  # noqa: E731
+    for _ in range(args.warmup + args.steps):
+        fn()
+    kernels.device_check(dev)
+    print(f"profile case {args.profile_case}: {args.warmup + args.steps} launches ok")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
+                    help="run a small case for ncu captures instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -316,6 +348,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.profile_case:
+        return run_profile_case(args)
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
