@@ -126,6 +126,26 @@ int gqa_decode_bf16(const void* q, const void* kcache, const void* vcache, const
                     int max_len, int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
                     float scale, int flags, gqa_stream_t stream);
 
+/* ---------------------------------------------------------------- allocation-free decode
+ * No counterpart in the reference: an addition for callers that cannot allocate
+ * device memory -- a plugin host that passes the library only its input and
+ * output buffers and owns all other device memory, a serving loop that must not
+ * call cudaMalloc/cudaFree (they synchronise the device), or a process whose
+ * memory pool is reserved in full up front.
+ * Same arguments and result as gqa_decode_bf16 minus the workspace: the split-KV
+ * partials go to a 16 MiB scratch array built into the library (one per GPU,
+ * held until the process exits; gqa_decode_noalloc_scratch_bytes() returns the
+ * size).  A request needing more than that (gqa_decode_workspace_size) returns
+ * GQA_ERR_WORKSPACE without launching.  Calls share the array: calls whose
+ * kernels overlap on the GPU race and give wrong results, so order them on one
+ * stream.  The first call on each device resolves the array's address; make it
+ * before any stream capture starts.                                            */
+size_t gqa_decode_noalloc_scratch_bytes(void);
+int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const void* vcache, const int32_t* lens,
+                            const int32_t* q_pos, const void* cos, const void* sin, void* o, int B, int max_len,
+                            int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
+                            float scale, int flags, gqa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

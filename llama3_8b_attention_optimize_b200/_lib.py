@@ -43,6 +43,9 @@ SIGNATURES = {
     "gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i]),
     "gqa_decode_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _i, _i, _i, _i, _f,
                              _i, _vp]),
+    "gqa_decode_noalloc_scratch_bytes": (_sz, []),
+    "gqa_decode_bf16_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _i,
+                                     _vp]),
 }
 
 

@@ -292,3 +292,76 @@ extern "C" int gqa_decode_bf16(const void* q, const void* kcache, const void* vc
   decode_combine_kernel<<<dim3(kv_head_count * kG, B), kD, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of gqa_decode_bf16.
+//
+// Some callers cannot allocate device memory: a plugin host that hands the
+// library only its own input and output buffers and owns every other byte of
+// device memory, a serving loop that must not call cudaMalloc/cudaFree because
+// those calls synchronise the device, or a process whose memory pool was
+// reserved in full before the model started.  For them the split-KV partials
+// live in a fixed scratch array compiled into this library instead of a
+// caller-provided workspace.
+//
+// Limits and sharing rules:
+//  - The scratch holds kNoAllocScratchBytes (16 MiB) per GPU; every GPU that
+//    loads the library keeps it for the life of the process.  A request whose
+//    partials need more (gqa_decode_workspace_size(B, Hq, max_len, split_len))
+//    is rejected with GQA_ERR_WORKSPACE before anything is launched.
+//  - All calls on a device share the one array, and it keeps the previous
+//    call's contents.  Nothing in it has to start at zero: every slot the
+//    combine step reads is written earlier in the same call.  Two calls whose
+//    kernels overlap on the GPU (different streams, no ordering between them)
+//    race on the array and produce wrong results; order them on one stream.
+//  - The first call on each device looks up the array's device address with
+//    cudaGetSymbolAddress (with that device current); make that first call
+//    before any stream capture begins.
+namespace gqa {
+namespace decode {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::atomic<float*> g_scratch_ptr[kMaxDevices];
+
+// Device address of g_decode_scratch on the current device (looked up once).
+// In host code the symbol name is only a host-side handle; kernels must be given
+// the address returned by cudaGetSymbolAddress.
+int scratch_address(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return GQA_ERR_UNSUPPORTED;
+  float* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_decode_scratch) != cudaSuccess || addr == nullptr) return GQA_ERR_CUDA;
+    p = static_cast<float*>(addr);
+    g_scratch_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return GQA_OK;
+}
+
+}  // namespace decode
+}  // namespace gqa
+
+extern "C" size_t gqa_decode_noalloc_scratch_bytes(void) { return gqa::decode::kNoAllocScratchBytes; }
+
+extern "C" int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const void* vcache, const int32_t* lens,
+                                       const int32_t* q_pos, const void* cos, const void* sin, void* o, int B,
+                                       int max_len, int Hq, int Hkv, int head_dim, int kv_head_begin,
+                                       int kv_head_count, int split_len, float scale, int flags,
+                                       gqa_stream_t stream) {
+  using namespace gqa::decode;
+  if (B <= 0 || Hq <= 0 || max_len <= 0 || split_len < 0) return GQA_ERR_INVALID_ARGUMENT;
+  const size_t need = gqa_decode_workspace_size(B, Hq, max_len, split_len);
+  if (need == 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (need > kNoAllocScratchBytes) return GQA_ERR_WORKSPACE;
+  float* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != GQA_OK) return rc;
+  return gqa_decode_bf16(q, kcache, vcache, lens, q_pos, cos, sin, o, scratch, kNoAllocScratchBytes, B, max_len, Hq,
+                         Hkv, head_dim, kv_head_begin, kv_head_count, split_len, scale, flags, stream);
+}
