@@ -4,8 +4,9 @@
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Workload (one step = one launch of the fused kernel over one batch):
-  causal GQA prefill, Hq=32, Hkv=8, d=128, seq 8192, bf16, RoPE (theta 5e5) applied
-  in the kernel to the raw Q/K; Q,K ~ 2.5*N(0,1), V ~ N(0,1) (seeded synthetic).
+  causal GQA prefill, Hq=32, Hkv=8, d=128, seq 8192, bf16, from un-rotated Q/K: RoPE
+  (theta 5e5) on K by one pre-pass kernel and on Q inside the fused kernel (--rope fused
+  rotates both inside the fused kernel); Q,K ~ 2.5*N(0,1), V ~ N(0,1) (seeded synthetic).
   N=1: batch 4 (the headline configuration).  N GPUs: batch 4N, rank r owns kv
   heads [8r/N, 8(r+1)/N) of every sequence (KV-head sharding, no collective), so the
   work per GPU is fixed ("weak" scaling).  Inputs (335 MB per rank) exceed L2.
@@ -213,7 +214,7 @@ def run_ours(args, world, rank, local):
     hq, hkv = sh.q_count, sh.kv_count
 
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    sess = PrefillSession(B, S_PREFILL, hq, hkv, D, causal=True, rope=True, device=dev)
+    sess = PrefillSession(B, S_PREFILL, hq, hkv, D, causal=True, rope=args.rope, device=dev)
     sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev) * 2.5)
     sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev) * 2.5)
     sess.v.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
@@ -287,14 +288,15 @@ def run_ours(args, world, rank, local):
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1); Q,K x2.5)",
-        "config": {"workload": "gqa_causal_prefill_fused_rope", "global_batch": B, "batch_per_gpu_equiv": B_PER_GPU,
+        "config": {"workload": "gqa_causal_prefill_from_unrotated_qk", "rope": args.rope,
+                   "global_batch": B, "batch_per_gpu_equiv": B_PER_GPU,
                    "seq_len": S_PREFILL, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
                    "parallelism": f"kv_head_shard{world}", "l2": "inputs 335 MB/rank > L2 (126 MB)"},
         "roofline": roof,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
                 "h2d_bytes_per_step": sess.h2d_bytes() * world, "d2h_bytes_per_step": sess.d2h_bytes() * world,
                 "path": "PrefillSession.run_host: pinned host Q/K/V -> device -> gqa_prefill_bf16 -> pinned host O"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * sess.launches_per_step(),
         "clocks": clk.summary(),
         "decode": {"metric": "split-KV GQA decode HBM GB/s", "value": dec_gbs, "unit": "GB/s", "ms_per_step": ms_dec,
                    "config": {"batch": dB, "max_len": DEC_LMAX, "lens": "U[1024,32768] seed 99",
@@ -315,7 +317,7 @@ def run_profile_case(args):
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(7)
     if args.profile_case == "prefill":
-        sess = PrefillSession(2, S_PREFILL, HQ, HKV, D, device=dev)
+        sess = PrefillSession(2, S_PREFILL, HQ, HKV, D, rope=args.rope, device=dev)
         sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev) * 2.5)
         sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev) * 2.5)
         sess.v.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
@@ -345,6 +347,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rope", choices=["prepass_k", "fused", "none"], default="prepass_k",
+                    help="prepass_k: K rotated once by its own kernel, Q rotated inside the fused kernel; "
+                         "fused: both rotated inside the fused kernel")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

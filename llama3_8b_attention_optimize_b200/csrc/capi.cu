@@ -78,3 +78,13 @@ extern "C" int gqa_prefill_bf16(const void* q, const void* k, const void* v, voi
   return launch_prefill(q, k, v, o, cos, sin, B, seq_len, Hq, Hkv, head_dim, kv_head_begin, kv_head_count, scale,
                         flags, stream);
 }
+
+// Diagnostic (not part of the public header): the fused prefill with a clock64 event
+// trace of one CTA written to `trace` (device buffer of 6*128*8 int64).
+extern "C" int gqa_prefill_trace_bf16(const void* q, const void* k, const void* v, void* o, const void* cos,
+                                      const void* sin, int B, int seq_len, int Hq, int Hkv, int head_dim,
+                                      int kv_head_begin, int kv_head_count, float scale, int flags,
+                                      long long* trace, int trace_block, gqa_stream_t stream) {
+  return launch_prefill(q, k, v, o, cos, sin, B, seq_len, Hq, Hkv, head_dim, kv_head_begin, kv_head_count, scale,
+                        flags, stream, trace, trace_block);
+}

@@ -33,6 +33,6 @@ int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {
 
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
-                   cudaStream_t stream);
+                   cudaStream_t stream, long long* trace = nullptr, int trace_block = -1);
 
 }  // namespace gqa

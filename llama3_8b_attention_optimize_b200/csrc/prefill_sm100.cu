@@ -12,17 +12,23 @@
 // positions (row r = head_in_group*32 + position_offset), so one K/V tile in shared
 // memory serves all 4 heads of the group (GQA by address, no KV duplication).
 //
-// Warp roles (12 warps):
-//   warps 0-3  softmax warpgroup for Q tile 0 (thread r owns TMEM lane / row r)
-//   warps 4-7  softmax warpgroup for Q tile 1
-//   warp 8     TMA producer (Q tiles, then K0 V0 K1 V1 ... into a 4-stage ring)
-//   warp 9     tcgen05.mma issuer (one elected thread) + TMEM allocator
-//   warps 10-11 RoPE of K tiles in shared memory (when FLAG_ROPE_K)
-// TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
-// P_t (bf16 pairs) overwrites the first 64 columns of S_t and feeds PV as the A operand.
+// Pipeline: each softmax thread copies its row of S_t (128 keys) from TMEM into
+// registers and releases S_t at once, so the tensor core computes S_t for the next
+// K tile while the softmax works; P_t (bf16) goes to shared memory and O_t += P_t V
+// runs with both operands in shared memory.  Softmax and both GEMMs overlap.
+//
+// Warp roles (20 warps):
+//   warps 0-15 four softmax warpgroups; warpgroup g serves Q tile g/2 and key/dim half
+//              g%2 (thread r owns TMEM lane / row r; the two halves of a row exchange
+//              their partial row max through shared memory)
+//   warp 16    TMA producer (Q tiles, then K0 K1 V0 K2 V1 ... into a 3-stage ring)
+//   warp 17    tcgen05.mma issuer (one elected thread) + TMEM allocator
+//   warps 18-19 RoPE of K tiles in shared memory (when FLAG_ROPE_K)
+// TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 //
 // Online softmax in the log2 domain: p = 2^(s*scale*log2e - m); the running max m is
-// only raised (and O rescaled) when a tile's max exceeds it by more than 8, so p <= 256.
+// only raised (and O rescaled) when a tile's max exceeds it by more than kRescaleLog2,
+// so p <= 2^16: with |v| < 2^16 and at most 2^17 keys, O stays below 2^49 (fp32-safe).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -34,32 +40,50 @@ namespace prefill {
 constexpr int kD = 128;
 constexpr int kG = 4;
 constexpr int kBM = 128;
-constexpr int kRowsPerHead = kBM / kG;  // 32
+constexpr int kRowsPerHead = kBM / kG;        // 32
 constexpr int kPosPerCta = 2 * kRowsPerHead;  // 64
-constexpr int kBN = 128;
-constexpr int kStages = 4;
-constexpr int kTileBytes = 128 * 128 * 2;
-constexpr int kHalfBytes = kTileBytes / 2;
-constexpr int kThreads = 384;
+constexpr int kBN = 128;                      // keys per K/V tile
+constexpr int kStages = 3;                    // K/V ring stages
+constexpr int kTileBytes = 128 * 128 * 2;     // Q, P, K and V tiles: 32 KB
+constexpr int kHalf = kTileBytes / 2;         // one 64-column swizzle block of 128 rows
+constexpr int kSoftmaxThreads = 512;  // warps 0-15
+constexpr float kRescaleLog2 = 16.0f;
+constexpr int kWarpProducer = 16;
+constexpr int kWarpMma = 17;
+constexpr int kWarpRope0 = 18;
+constexpr int kThreads = 640;
 
+// The 1024-byte-aligned tiles come first; the dynamic shared-memory base is
+// 1024-byte aligned (checked at run time), so no alignment slack is allocated.
 constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + 2 * kTileBytes;
+constexpr int kOffP = kOffQ + 2 * kTileBytes;
+constexpr int kOffKV = kOffP + 2 * kTileBytes;
 constexpr int kOffBar = kOffKV + kStages * kTileBytes;
-constexpr int kNumBars = 24;
-constexpr int kOffTmemPtr = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffTmemPtr + 16 + 1024;
+constexpr int kNumBars = 32;
+constexpr int kOffX = kOffBar + kNumBars * 8;        // row-max / row-sum exchange [2 tiles][2 halves][128]
+constexpr int kOffTmemPtr = kOffX + 2 * 2 * 128 * 4;
+constexpr int kSmemBytes = kOffTmemPtr + 16;
+static_assert(kSmemBytes <= 232448, "shared memory over the per-block limit");
 
 enum : int {
   B_QFULL = 0,     // [2]  TMA Q landed
   B_QREADY = 2,    // [2]  Q (rotated) visible to the tensor core, 128 arrivals
-  B_KVFULL = 4,    // [4]  TMA K/V stage landed
-  B_KVEMPTY = 8,   // [4]  MMAs reading the stage completed
-  B_KREADY = 12,   // [4]  K stage rotated, 64 arrivals
-  B_SFULL = 16,    // [2]  S_t = Q_t K^T complete
-  B_PREADY = 18,   // [2]  P_t in TMEM (and O_t rescaled), 128 arrivals
-  B_ODONE = 20,    // [2]  O_t += P_t V complete
+  B_KVFULL = 4,    // [3]  TMA K/V stage landed
+  B_KVEMPTY = 7,   // [3]  MMAs reading the stage completed
+  B_KREADY = 10,   // [4]  K tile j rotated (slot j % 4), 64 arrivals
+  B_SFULL = 14,    // [2]  S_t = Q_t K^T complete
+  B_SFREE = 16,    // [1]  S_0 and S_1 copied to registers (512 arrivals)
+  B_PREADY = 18,   // [1]  P_0 and P_1 in shared memory, O rescaled (512 arrivals)
+  B_PVDONE = 20,   // [2]  O_t += P_t V complete (P_t buffer free)
   B_DRAIN = 22,    // [1]  every MMA of the CTA complete
 };
+constexpr int kKReadySlots = 4;
+
+// Load order of the K/V ring: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1).  With K
+// one tile ahead, every stage a load reuses was released an iteration earlier (K(j+1)
+// reuses V(j-2)'s stage, V(j) reuses K(j)'s), so a 3-stage ring never stalls the MMAs.
+__device__ __forceinline__ int load_idx_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int load_idx_v(int j, int n) { return j + 1 < n ? 2 * j + 2 : 2 * n - 1; }
 
 enum : int {  // error sites reported through g_gqa_dev_error
   SITE_PRODUCER = 0x101,
@@ -68,6 +92,7 @@ enum : int {  // error sites reported through g_gqa_dev_error
   SITE_ROPEK = 0x104,
   SITE_EPILOGUE = 0x105,
   SITE_DRAIN = 0x106,
+  SITE_SMEM_ALIGN = 0x107,
 };
 
 struct Params {
@@ -76,51 +101,139 @@ struct Params {
   float scale_log2;
   const uint16_t* cos;  // [>= S][128] bf16 (cat(freqs, freqs) layout)
   const uint16_t* sin;
+  long long* trace;  // diagnostic event trace of one CTA (nullptr = off)
+  int trace_block;
 };
+
+// Diagnostic trace: clock64 stamps [role][iteration][event] for CTA trace_block.
+constexpr int kTraceIters = 128;
+constexpr int kTraceRoles = 6;
+constexpr int kTraceEv = 8;
+#define PF_TRACE(role, it, ev)                                                                        \
+  do {                                                                                                \
+    if (kTrace && tr) tr[((role) * kTraceIters + min((it), kTraceIters - 1)) * kTraceEv + (ev)] = clock64(); \
+  } while (0)
 
 __device__ __forceinline__ uint32_t colS(int t) { return static_cast<uint32_t>(t * 128); }
 __device__ __forceinline__ uint32_t colO(int t) { return static_cast<uint32_t>(256 + t * 128); }
 
-// Rotate one 128-element row held in a K-major SWIZZLE_128B tile (two 64-column
-// blocks 16 KB apart; dims d and d+64 sit at the same offset in the two blocks).
-__device__ __forceinline__ void rope_row_smem(uint8_t* tile, int row, const uint16_t* cos_row,
-                                              const uint16_t* sin_row) {
-#pragma unroll
-  for (int ch = 0; ch < 8; ++ch) {
+// Byte offset of 16-byte chunk c (elements 8c..8c+7) of row r in a 128x128 bf16
+// K-major SWIZZLE_128B tile (two 64-column blocks of 128 rows x 128 B).
+__device__ __forceinline__ int sw128_chunk(int r, int c) {
+  return (c >> 3) * kHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void rope_pair(uint32_t& xa, uint32_t& xb, uint32_t c, uint32_t s) {
+  // y[d] = x[d]*cos - x[d+64]*sin ; y[d+64] = x[d+64]*cos + x[d]*sin (products are exact)
+  const float x0l = bf16_lo(xa), x0h = bf16_hi(xa), x1l = bf16_lo(xb), x1h = bf16_hi(xb);
+  const float cl = bf16_lo(c), chh = bf16_hi(c), sl = bf16_lo(s), shh = bf16_hi(s);
+  const float y0l = __fadd_rn(__fmul_rn(x0l, cl), -__fmul_rn(x1l, sl));
+  const float y0h = __fadd_rn(__fmul_rn(x0h, chh), -__fmul_rn(x1h, shh));
+  const float y1l = __fadd_rn(__fmul_rn(x1l, cl), __fmul_rn(x0l, sl));
+  const float y1h = __fadd_rn(__fmul_rn(x1h, chh), __fmul_rn(x0h, shh));
+  xa = pack_bf16x2(y0l, y0h);
+  xb = pack_bf16x2(y1l, y1h);
+}
+
+// Rotate chunk pairs [c0, c0+4) of one row (half of the row's 8 pairs).
+__device__ __forceinline__ void rope_row_smem_part(uint8_t* tile, int half, int row, const uint16_t* cos_row,
+                                                   const uint16_t* sin_row, int c0) {
+#pragma unroll 2
+  for (int ch = c0; ch < c0 + 4; ++ch) {
     const int off = row * 128 + ((ch ^ (row & 7)) << 4);
     uint4* pa = reinterpret_cast<uint4*>(tile + off);
-    uint4* pb = reinterpret_cast<uint4*>(tile + kHalfBytes + off);
+    uint4* pb = reinterpret_cast<uint4*>(tile + half + off);
     uint4 a = *pa, b = *pb;
     const uint4 c = __ldg(reinterpret_cast<const uint4*>(cos_row + ch * 8));
     const uint4 s = __ldg(reinterpret_cast<const uint4*>(sin_row + ch * 8));
-    uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-    uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
-    const uint32_t* cw = reinterpret_cast<const uint32_t*>(&c);
-    const uint32_t* sw = reinterpret_cast<const uint32_t*>(&s);
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      float x0l = bf16_lo(aw[w]), x0h = bf16_hi(aw[w]);
-      float x1l = bf16_lo(bw[w]), x1h = bf16_hi(bw[w]);
-      float cl = bf16_lo(cw[w]), chh = bf16_hi(cw[w]);
-      float sl = bf16_lo(sw[w]), shh = bf16_hi(sw[w]);
-      // y[d] = x[d]*cos - x[d+64]*sin ; y[d+64] = x[d+64]*cos + x[d]*sin (products are exact)
-      float y0l = __fadd_rn(__fmul_rn(x0l, cl), -__fmul_rn(x1l, sl));
-      float y0h = __fadd_rn(__fmul_rn(x0h, chh), -__fmul_rn(x1h, shh));
-      float y1l = __fadd_rn(__fmul_rn(x1l, cl), __fmul_rn(x0l, sl));
-      float y1h = __fadd_rn(__fmul_rn(x1h, chh), __fmul_rn(x0h, shh));
-      aw[w] = pack_bf16x2(y0l, y0h);
-      bw[w] = pack_bf16x2(y1l, y1h);
-    }
+    rope_pair(a.x, b.x, c.x, s.x);
+    rope_pair(a.y, b.y, c.y, s.y);
+    rope_pair(a.z, b.z, c.z, s.z);
+    rope_pair(a.w, b.w, c.w, s.w);
     *pa = a;
     *pb = b;
   }
 }
 
+// Rotate one 128-element row held in a K-major SWIZZLE_128B tile made of two
+// 64-dim blocks `half` bytes apart (dims d and d+64 sit at the same offset in the
+// two blocks).
+__device__ __forceinline__ void rope_row_smem(uint8_t* tile, int half, int row, const uint16_t* cos_row,
+                                              const uint16_t* sin_row) {
+#pragma unroll 2
+  for (int ch = 0; ch < 8; ++ch) {
+    const int off = row * 128 + ((ch ^ (row & 7)) << 4);
+    uint4* pa = reinterpret_cast<uint4*>(tile + off);
+    uint4* pb = reinterpret_cast<uint4*>(tile + half + off);
+    uint4 a = *pa, b = *pb;
+    const uint4 c = __ldg(reinterpret_cast<const uint4*>(cos_row + ch * 8));
+    const uint4 s = __ldg(reinterpret_cast<const uint4*>(sin_row + ch * 8));
+    rope_pair(a.x, b.x, c.x, s.x);
+    rope_pair(a.y, b.y, c.y, s.y);
+    rope_pair(a.z, b.z, c.z, s.z);
+    rope_pair(a.w, b.w, c.w, s.w);
+    *pa = a;
+    *pb = b;
+  }
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA pipe for a pair: x = n + f with n = round(x) (added-constant trick,
+// exact for |x| < 2^22), 2^f by a cubic on [-1/2, 1/2] (relative error 7.5e-5, a
+// near-minimax fit of 2^f made for this kernel), and 2^n added to the exponent
+// field.  x is clamped to >= -126 so the result stays a normal number.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261114f, c3 = 0.05517167f;
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 q = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+  q = __ffma2_rn(q, f, make_float2(c1, c1));
+  q = __ffma2_rn(q, f, make_float2(c0, c0));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// One 32-column chunk of S -> 16 packed bf16 pairs of p = 2^(s*scale_log2 - m) at
+// out[base..base+16); acc += the bf16-rounded p.
+template <bool kEmulate>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[32], uint32_t (&out)[32], int base, float2 sc2,
+                                          float2 nm2, float2& acc) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), sc2, nm2);
+    float2 e;
+    if (kEmulate && (i & 3) == 3) {
+      e = exp2_poly2(x);
+    } else {
+      e.x = ex2_approx(x.x);
+      e.y = ex2_approx(x.y);
+    }
+    const uint32_t w = pack_bf16x2(e.x, e.y);
+    out[base + i] = w;
+    // the row sum uses the bf16 values PV multiplies, so O / l normalises exactly them
+    acc = __fadd2_rn(acc, make_float2(bf16_lo(w), bf16_hi(w)));
+  }
+}
+
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // uniform across the CTA: leave before any barrier
+    if (threadIdx.x == 0) record_error(SITE_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -142,28 +255,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int zk = b * p.Hkv + kvh;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(B_QFULL + 0), 1);
-    mbar_init(bar(B_QFULL + 1), 1);
-    mbar_init(bar(B_QREADY + 0), 128);
-    mbar_init(bar(B_QREADY + 1), 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(B_QFULL + t), 1);
+      mbar_init(bar(B_QREADY + t), 256);
+      mbar_init(bar(B_SFULL + t), 1);
+
+      mbar_init(bar(B_PVDONE + t), 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(B_KVFULL + s), 1);
       mbar_init(bar(B_KVEMPTY + s), 1);
-      mbar_init(bar(B_KREADY + s), 64);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(B_SFULL + t), 1);
-      mbar_init(bar(B_PREADY + t), 128);
-      mbar_init(bar(B_ODONE + t), 1);
-    }
+    for (int k = 0; k < kKReadySlots; ++k) mbar_init(bar(B_KREADY + k), 64);
+    mbar_init(bar(B_SFREE), kSoftmaxThreads);
+    mbar_init(bar(B_PREADY), kSoftmaxThreads);
     mbar_init(bar(B_DRAIN), 1);
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == kWarpMma) {
     tmem_alloc(sbase + kOffTmemPtr, 512);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kWarpProducer && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -173,15 +286,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmemPtr);
+  long long* tr = (kTrace && static_cast<int>(blockIdx.x) == p.trace_block) ? p.trace : nullptr;
+  if (threadIdx.x == 0) PF_TRACE(5, 0, 0);
 
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       for (int t = 0; t < 2; ++t) {
         const uint32_t dst = sbase + kOffQ + t * kTileBytes;
         mbar_expect_tx(bar(B_QFULL + t), kTileBytes);
         tma_load_3d(dst, &tmQ, bar(B_QFULL + t), 0, cta_p0 + t * kRowsPerHead, zq);
-        tma_load_3d(dst + kHalfBytes, &tmQ, bar(B_QFULL + t), 64, cta_p0 + t * kRowsPerHead, zq);
+        tma_load_3d(dst + kHalf, &tmQ, bar(B_QFULL + t), 64, cta_p0 + t * kRowsPerHead, zq);
       }
       const int nloads = 2 * n_kv;
       int issued = 0;
@@ -190,12 +305,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % kStages, r = i / kStages;
         if (r > 0) ok = mbar_wait(bar(B_KVEMPTY + s), (r - 1) & 1, SITE_PRODUCER);
         if (!ok) break;
-        const int j = i >> 1;
-        const void* map = (i & 1) ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
+        // i -> (tile, K or V) in the K-ahead order
+        const bool is_v = (i == nloads - 1) || (i >= 2 && (i & 1) == 0);
+        const int j = i == 0 ? 0 : (is_v ? (i == nloads - 1 ? n_kv - 1 : (i - 2) >> 1) : (i + 1) >> 1);
+        const void* map = is_v ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
         const uint32_t dst = sbase + kOffKV + s * kTileBytes;
         mbar_expect_tx(bar(B_KVFULL + s), kTileBytes);
         tma_load_3d(dst, map, bar(B_KVFULL + s), 0, j * kBN, zk);
-        tma_load_3d(dst + kHalfBytes, map, bar(B_KVFULL + s), 64, j * kBN, zk);
+        tma_load_3d(dst + kHalf, map, bar(B_KVFULL + s), 64, j * kBN, zk);
+        PF_TRACE(0, j, is_v ? 1 : 0);
         issued = i + 1;
       }
       // Drain: every load this thread issued must land before the CTA may exit.
@@ -205,35 +323,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(B_QFULL + 1), 0, SITE_DRAIN);
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdQK = idesc_bf16_f32(128, 128, false);
-      constexpr uint32_t kIdPV = idesc_bf16_f32(128, 128, true);
+      constexpr uint32_t kIdQK = idesc_bf16_f32(128, kBN, false);
+      constexpr uint32_t kIdPV = idesc_bf16_f32(128, kD, true);
+      // Descriptor halves computed once; each MMA adds a compile-time offset (in
+      // 16-byte units) to the low word.  K-major operands (Q, K, P): LBO unused;
+      // V is MN-major with its two 64-dim blocks kHalf apart (LBO = kHalf).
+      constexpr uint32_t kHi = sdesc_hi_sw128(1024);
+      const uint32_t q_lo = sdesc_lo(sbase + kOffQ, 16);
+      const uint32_t p_lo = sdesc_lo(sbase + kOffP, 16);
+      const uint32_t kv_lo = sdesc_lo(sbase + kOffKV, 16);
+      const uint32_t v_lo = sdesc_lo(sbase + kOffKV, kHalf);
+      constexpr uint32_t kTile16 = kTileBytes / 16;
+      // S_t = Q_t K^T over d = 128 (8 k-steps of 16; both operands K-major SW128)
       auto issue_qk = [&](int t, int s) {
-        const uint32_t qa = sbase + kOffQ + t * kTileBytes;
-        const uint32_t ka = sbase + kOffKV + s * kTileBytes;
+        const uint32_t a0 = q_lo + t * kTile16, b0 = kv_lo + s * kTile16;
+        const uint32_t d = tmem + colS(t);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_ss(tmem + colS(t), sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), kIdQK,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * kHalf + (kk & 3) * 32) / 16;
+          umma_ss_lohi(d, a0 + off, b0 + off, kHi, kIdQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int t, int s, bool acc) {
-        const uint32_t va = sbase + kOffKV + s * kTileBytes;
+      // O_t (+)= P_t V over 128 keys (8 k-steps; P K-major SW128, V MN-major SW128)
+      auto issue_pv = [&](int t, int s, uint32_t acc) {
+        const uint32_t a0 = p_lo + t * kTile16, b0 = v_lo + s * kTile16;
+        const uint32_t d = tmem + colO(t);
+        umma_ss_lohi(d, a0, b0, kHi, kIdPV, acc);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(tmem + colO(t), tmem + colS(t) + kk * 8, sdesc_sw128(va + kk * 2048, kHalfBytes, 1024), kIdPV,
-                  (acc || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < 8; ++kk) {
+          const uint32_t off = ((kk >> 2) * kHalf + (kk & 3) * 32) / 16;
+          umma_ss_lohi(d, a0 + off, b0 + kk * (2048 / 16), kHi, kIdPV, 1u);
         }
       };
-      auto wait_k = [&](int i) -> bool {
-        const int s = i % kStages, r = i / kStages;
-        return mbar_wait(bar((rope_k ? B_KREADY : B_KVFULL) + s), r & 1, SITE_MMA);
+      auto wait_k = [&](int j) -> bool {  // K tile j landed (and rotated)
+        if (rope_k) return mbar_wait_spin(bar(B_KREADY + j % kKReadySlots), (j / kKReadySlots) & 1, SITE_MMA);
+        const int i = load_idx_k(j);
+        return mbar_wait_spin(bar(B_KVFULL + i % kStages), (i / kStages) & 1, SITE_MMA);
       };
-      bool ok = mbar_wait(bar(B_QREADY + 0), 0, SITE_MMA) && mbar_wait(bar(B_QREADY + 1), 0, SITE_MMA);
-      if (ok) ok = wait_k(0);
+      bool ok = mbar_wait_spin(bar(B_QREADY + 0), 0, SITE_MMA) && mbar_wait_spin(bar(B_QREADY + 1), 0, SITE_MMA) &&
+                wait_k(0);
       if (ok) {
         tc_fence_after();
         issue_qk(0, 0);
@@ -243,70 +374,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(bar(B_KVEMPTY + 0));
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int iv = 2 * j + 1, sv = iv % kStages;
-        const int ik = 2 * j + 2, sk = ik % kStages;
-        const bool more = (j + 1) < n_kv;
-        ok = mbar_wait(bar(B_KVFULL + sv), (iv / kStages) & 1, SITE_MMA) &&
-             mbar_wait(bar(B_PREADY + 0), j & 1, SITE_MMA);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(0, sv, j > 0);
-        umma_commit(bar(B_ODONE + 0));
-        if (more) {
-          ok = wait_k(ik);
+        PF_TRACE(1, j, 0);
+        if (j + 1 < n_kv) {
+          // next S as soon as the softmax warps hold S(j) in registers
+          const int sk = load_idx_k(j + 1) % kStages;
+          ok = wait_k(j + 1) && mbar_wait_spin(bar(B_SFREE), j & 1, SITE_MMA);
           if (!ok) break;
+          PF_TRACE(1, j, 1);
           tc_fence_after();
           issue_qk(0, sk);
           umma_commit(bar(B_SFULL + 0));
-        }
-        ok = mbar_wait(bar(B_PREADY + 1), j & 1, SITE_MMA);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(1, sv, j > 0);
-        umma_commit(bar(B_ODONE + 1));
-        umma_commit(bar(B_KVEMPTY + sv));
-        if (more) {
+          PF_TRACE(1, j, 2);
           issue_qk(1, sk);
           umma_commit(bar(B_SFULL + 1));
           umma_commit(bar(B_KVEMPTY + sk));
+          PF_TRACE(1, j, 3);
         }
+        const int iv = load_idx_v(j, n_kv), sv = iv % kStages;
+        ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1, SITE_MMA) &&
+             mbar_wait_spin(bar(B_PREADY), j & 1, SITE_MMA);
+        if (!ok) break;
+        PF_TRACE(1, j, 4);
+        tc_fence_after();
+        issue_pv(0, sv, j > 0 ? 1u : 0u);
+        umma_commit(bar(B_PVDONE + 0));
+        PF_TRACE(1, j, 5);
+        PF_TRACE(1, j, 6);
+        tc_fence_after();
+        issue_pv(1, sv, j > 0 ? 1u : 0u);
+        umma_commit(bar(B_PVDONE + 1));
+        umma_commit(bar(B_KVEMPTY + sv));
+        PF_TRACE(1, j, 7);
       }
       umma_commit(bar(B_DRAIN));
       mbar_wait(bar(B_DRAIN), 0, SITE_DRAIN);
     }
     __syncwarp();
-  } else if (warp >= 10) {
+  } else if (warp >= kWarpRope0) {
     // ------------------------------------------------------------ RoPE of K tiles
     if (rope_k) {
-      const int tid = threadIdx.x - 320;  // 0..63
+      const int tid = threadIdx.x - kWarpRope0 * 32;  // 0..63
       for (int j = 0; j < n_kv; ++j) {
-        const int i = 2 * j, s = i % kStages, r = i / kStages;
+        const int i = load_idx_k(j), s = i % kStages, r = i / kStages;
         if (!mbar_wait(bar(B_KVFULL + s), r & 1, SITE_ROPEK)) break;
+        if (tid == 0) PF_TRACE(4, j, 0);
         uint8_t* tile = smem + kOffKV + s * kTileBytes;
 #pragma unroll 1
         for (int rr = tid; rr < kBN; rr += 64) {
           const int key = j * kBN + rr;
-          if (key < p.S) rope_row_smem(tile, rr, p.cos + static_cast<size_t>(key) * kD, p.sin + static_cast<size_t>(key) * kD);
+          if (key < p.S)
+            rope_row_smem(tile, kHalf, rr, p.cos + static_cast<size_t>(key) * kD, p.sin + static_cast<size_t>(key) * kD);
         }
         fence_proxy_async_smem();
-        mbar_arrive(bar(B_KREADY + s));
+        if (tid == 0) PF_TRACE(4, j, 1);
+        mbar_arrive(bar(B_KREADY + j % kKReadySlots));
       }
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
-    const int t = warp >> 2;             // Q tile
+    const int g = warp >> 2;             // warpgroup 0..3
+    const int t = g >> 1;                // Q tile
+    const int h = g & 1;                 // keys [64h, 64h+64) of each K tile; O dims [64h, 64h+64)
     const int r = threadIdx.x & 127;     // row in tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + colS(t);
-    const uint32_t tO = tmem + lane_off + colO(t);
+    const uint32_t tS = tmem + lane_off + colS(t) + 64 * h;
+    const uint32_t tO = tmem + lane_off + colO(t) + 64 * h;
     const int p0 = cta_p0 + t * kRowsPerHead;
     const int qpos = p0 + (r & (kRowsPerHead - 1));
     uint8_t* qtile = smem + kOffQ + t * kTileBytes;
+    uint8_t* ptile = smem + kOffP + t * kTileBytes;
+    float* xchg = reinterpret_cast<float*>(smem + kOffX) + t * 256;  // [half][row]
+    const int bar_x = 1 + t;     // named barrier: both halves of tile t (256 threads)
+    const int bar_free = 3 + t;  // named barrier: exchange slots may be rewritten
     const float sl2 = p.scale_log2;
 
     bool ok = mbar_wait(bar(B_QFULL + t), 0, SITE_SOFTMAX);
-    if (ok && rope_q && qpos < p.S)
-      rope_row_smem(qtile, r, p.cos + static_cast<size_t>(qpos) * kD, p.sin + static_cast<size_t>(qpos) * kD);
+    if (ok && rope_q && qpos < p.S)  // each half rotates 4 of the row's 8 chunk pairs
+      rope_row_smem_part(qtile, kHalf, r, p.cos + static_cast<size_t>(qpos) * kD,
+                         p.sin + static_cast<size_t>(qpos) * kD, 4 * h);
     fence_proxy_async_smem();
     mbar_arrive(bar(B_QREADY + t));
     ok = __all_sync(0xffffffffu, ok);
@@ -314,79 +459,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     // last key this row may attend
     const int lim = causal ? min(qpos, p.S - 1) : p.S - 1;
     float m_run = -INFINITY, l_run = 0.0f;
-    for (int j = 0; ok && j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + t), j & 1, SITE_SOFTMAX));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t s0[32], s1[32], s2[32], s3[32];
-      tmem_ld32(tS + 0, s0);
-      tmem_ld32(tS + 32, s1);
-      tmem_ld32(tS + 64, s2);
-      tmem_ld32(tS + 96, s3);
-      tmem_wait_ld_dep(s0);
-      reg_dep(s1);
-      reg_dep(s2);
-      reg_dep(s3);
-      const int key0 = j * kBN;
-      const int rel = lim - key0;  // columns > rel are masked
-      if (rel < kBN - 1) {
+    // Every warp of the tile runs all n_kv iterations and meets every named barrier,
+    // even after a bounded wait failed (ok == false only skips the work), so the two
+    // halves of a tile can never wait on each other forever.
+    for (int j = 0; j < n_kv; ++j) {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + t), j & 1, SITE_SOFTMAX));
+      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 0);
+      uint32_t s0[32], s1[32];
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(tS + 0, s0);
+        tmem_ld32(tS + 32, s1);
+        tmem_wait_ld_dep(s0);
+        reg_dep(s1);
+        tc_fence_before();
+        mbar_arrive(bar(B_SFREE));  // S_t may now be overwritten by the next QK^T
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s0[k] = s1[k] = 0xFF800000u;
+      }
+
+      const int rel = lim - j * kBN - 64 * h;  // columns (of this half) > rel are masked
+      if (rel < 63) {
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
           if (k > rel) s0[k] = 0xFF800000u;
           if (k + 32 > rel) s1[k] = 0xFF800000u;
-          if (k + 64 > rel) s2[k] = 0xFF800000u;
-          if (k + 96 > rel) s3[k] = 0xFF800000u;
         }
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        mx0 = fmaxf(mx0, __uint_as_float(s0[k]));
-        mx1 = fmaxf(mx1, __uint_as_float(s1[k]));
-        mx2 = fmaxf(mx2, __uint_as_float(s2[k]));
-        mx3 = fmaxf(mx3, __uint_as_float(s3[k]));
+      for (int k = 0; k < 32; k += 2) {
+        mx0 = fmax3(mx0, __uint_as_float(s0[k]), __uint_as_float(s0[k + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(s1[k]), __uint_as_float(s1[k + 1]));
       }
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      // row max over both halves: slot [h][r] <-> [1-h][r]
+      named_bar_sync(bar_free, 256);  // everyone has read the previous iteration's slots
+      xchg[h * 128 + r] = fmaxf(mx0, mx1);
+      named_bar_sync(bar_x, 256);
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), xchg[(1 - h) * 128 + r]) * sl2;
+      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 1);
       const float m_new = fmaxf(m_run, m_tile);
-      const bool need = m_new > m_run + 8.0f;
+      const bool need = m_new > m_run + kRescaleLog2;
       const float m_use = need ? m_new : m_run;
       const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
       const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
 
-      uint32_t pa[32], pb[32];
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        float e0 = ex2_approx(fmaf(__uint_as_float(s0[k]), sl2, -moff));
-        float e1 = ex2_approx(fmaf(__uint_as_float(s0[k + 1]), sl2, -moff));
-        float e2 = ex2_approx(fmaf(__uint_as_float(s1[k]), sl2, -moff));
-        float e3 = ex2_approx(fmaf(__uint_as_float(s1[k + 1]), sl2, -moff));
-        float e4 = ex2_approx(fmaf(__uint_as_float(s2[k]), sl2, -moff));
-        float e5 = ex2_approx(fmaf(__uint_as_float(s2[k + 1]), sl2, -moff));
-        float e6 = ex2_approx(fmaf(__uint_as_float(s3[k]), sl2, -moff));
-        float e7 = ex2_approx(fmaf(__uint_as_float(s3[k + 1]), sl2, -moff));
-        const uint32_t w0 = pack_bf16x2(e0, e1), w1 = pack_bf16x2(e2, e3);
-        const uint32_t w2 = pack_bf16x2(e4, e5), w3 = pack_bf16x2(e6, e7);
-        pa[k >> 1] = w0;
-        pa[16 + (k >> 1)] = w1;
-        pb[k >> 1] = w2;
-        pb[16 + (k >> 1)] = w3;
-        // the row sum uses the bf16 values PV multiplies, so O / l normalises exactly them
-        sum0 += bf16_lo(w0) + bf16_hi(w0);
-        sum1 += bf16_lo(w1) + bf16_hi(w1);
-        sum2 += bf16_lo(w2) + bf16_hi(w2);
-        sum3 += bf16_lo(w3) + bf16_hi(w3);
+      uint32_t pw[32];
+      float2 sum = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-moff, -moff);
+      // Chunks with no masked entry evaluate a quarter of the exponentials on the FMA
+      // pipe; masked chunks use ex2 only, so masked entries stay exactly zero.
+      if (rel >= 63) {
+        exp_chunk<true>(s0, pw, 0, sc2, nm2, sum);
+        exp_chunk<true>(s1, pw, 16, sc2, nm2, sumb);
+      } else {
+        exp_chunk<false>(s0, pw, 0, sc2, nm2, sum);
+        exp_chunk<false>(s1, pw, 16, sc2, nm2, sumb);
       }
-      tmem_st32(tS + 0, pa);
-      tmem_st32(tS + 32, pb);
 
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O_t must be quiescent: PV of the previous tile finished.
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + t), (j - 1) & 1, SITE_SOFTMAX));
-        if (ok) {
+      // P_t's buffer (and O_t) are free once the previous PV finished.
+      if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (j - 1) & 1, SITE_SOFTMAX));
+      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 2);
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(ptile + sw128_chunk(r, 8 * h + c)) =
+              make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+        fence_proxy_async_smem();
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + 32 * c, o);
             tmem_wait_ld_dep(o);
@@ -394,44 +538,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
             tmem_st32(tO + 32 * c, o);
           }
+          tmem_wait_st();
         }
+        tc_fence_before();
+        mbar_arrive(bar(B_PREADY));
       }
-      tmem_wait_st();
-      l_run = l_run * alpha + ((sum0 + sum1) + (sum2 + sum3));
+      l_run = l_run * alpha + ((sum.x + sum.y) + (sumb.x + sumb.y));
       m_run = m_use;
-      tc_fence_before();
-      mbar_arrive(bar(B_PREADY + t));
+      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 3);
     }
 
     // ---- epilogue: O / l -> bf16 -> (reuse the Q tile smem) -> TMA store
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + t), (n_kv - 1) & 1, SITE_EPILOGUE));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (n_kv - 1) & 1, SITE_EPILOGUE));
+    named_bar_sync(bar_free, 256);
+    xchg[h * 128 + r] = l_run;
+    named_bar_sync(bar_x, 256);
+    const float l_tot = l_run + xchg[(1 - h) * 128 + r];
     if (ok) {
       tc_fence_after();
-      const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const float inv_l = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld32(tO + 32 * c, o);
         tmem_wait_ld_dep(o);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte chunk
-          const int dc = c * 4 + q;    // chunk index over d (0..15)
           uint4 v;
           v.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
           v.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
           v.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
           v.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
-          const int cb = dc >> 3, ch = dc & 7;
-          *reinterpret_cast<uint4*>(qtile + cb * kHalfBytes + r * 128 + ((ch ^ (r & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(qtile + sw128_chunk(r, 8 * h + c * 4 + q)) = v;
         }
       }
     }
     fence_proxy_async_smem();
-    named_bar_sync(1 + t, 128);
-    if (ok && r == 0 && p0 < p.S) {  // a tile starting past the sequence has nothing to store
+    named_bar_sync(bar_x, 256);
+    if (ok && h == 0 && r == 0 && p0 < p.S) {  // a tile starting past the sequence has nothing to store
       const uint32_t src = sbase + kOffQ + t * kTileBytes;
       tma_store_3d(&tmO, src, 0, p0, zq);
-      tma_store_3d(&tmO, src + kHalfBytes, 64, p0, zq);
+      tma_store_3d(&tmO, src + kHalf, 64, p0, zq);
       bulk_commit();
       bulk_wait0();
     }
@@ -439,8 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- teardown: everyone done with TMEM and shared memory
   tc_fence_before();
-  named_bar_sync(3, kThreads);
-  if (warp == 9) {
+  named_bar_sync(5, kThreads);
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -451,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ host side
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, long long* trace, int trace_block) {
   using namespace prefill;
   if (!q || !k || !v || !o) return GQA_ERR_INVALID_ARGUMENT;
   if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0) return GQA_ERR_INVALID_ARGUMENT;
@@ -468,13 +615,16 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
 
   CUtensorMap tmQ, tmK, tmV, tmO;
   int rc;
-  if ((rc = make_tmap_3d_bf16(&tmQ, q, kD, S, static_cast<long long>(B) * Hq, 64, kRowsPerHead, kG)) != GQA_OK) return rc;
+  if ((rc = make_tmap_3d_bf16(&tmQ, q, kD, S, static_cast<long long>(B) * Hq, 64, kRowsPerHead, kG)) != GQA_OK)
+    return rc;
   if ((rc = make_tmap_3d_bf16(&tmK, k, kD, S, static_cast<long long>(B) * Hkv, 64, kBN, 1)) != GQA_OK) return rc;
   if ((rc = make_tmap_3d_bf16(&tmV, v, kD, S, static_cast<long long>(B) * Hkv, 64, kBN, 1)) != GQA_OK) return rc;
-  if ((rc = make_tmap_3d_bf16(&tmO, o, kD, S, static_cast<long long>(B) * Hq, 64, kRowsPerHead, kG)) != GQA_OK) return rc;
+  if ((rc = make_tmap_3d_bf16(&tmO, o, kD, S, static_cast<long long>(B) * Hq, 64, kRowsPerHead, kG)) != GQA_OK)
+    return rc;
 
-  static std::atomic<uint64_t> attr_done{0};
-  if ((rc = ensure_smem_attr(prefill_kernel, kSmemBytes, attr_done)) != GQA_OK) return rc;
+  static std::atomic<uint64_t> attr_done{0}, attr_done_tr{0};
+  if ((rc = ensure_smem_attr(prefill_kernel<false>, kSmemBytes, attr_done)) != GQA_OK) return rc;
+  if (trace && (rc = ensure_smem_attr(prefill_kernel<true>, kSmemBytes, attr_done_tr)) != GQA_OK) return rc;
   Params p;
   p.B = B;
   p.S = S;
@@ -487,7 +637,12 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   p.scale_log2 = scale * 1.4426950408889634f;
   p.cos = static_cast<const uint16_t*>(cos);
   p.sin = static_cast<const uint16_t*>(sin);
-  prefill_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
+  p.trace = trace;
+  p.trace_block = trace_block;
+  if (trace)
+    prefill_kernel<true><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
+  else
+    prefill_kernel<false><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 

@@ -13,16 +13,35 @@ import torch
 from . import kernels
 
 
+ROPE_MODES = ("prepass_k", "fused", "none")
+
+
 class PrefillSession:
+    """Device buffers + RoPE tables for one prefill shape.
+
+    rope = "prepass_k" (default): K is rotated once by gqa_rope_bf16 into a session
+           buffer, Q is rotated on load inside the fused kernel.
+    rope = "fused":     both rotated inside the fused kernel (every CTA that reads a K
+           tile rotates it again; no extra buffer).
+    rope = "none":      inputs already rotated.
+    """
+
     def __init__(self, B: int, S: int, Hq: int, Hkv: int, head_dim: int = 128, *, causal: bool = True,
-                 rope: bool = True, theta: float = kernels.ROPE_THETA, device=None):
+                 rope: str = "prepass_k", theta: float = kernels.ROPE_THETA, device=None):
+        if rope not in ROPE_MODES:
+            raise ValueError(f"rope must be one of {ROPE_MODES}")
         self.device = torch.device(device or "cuda")
         self.shape_q = (B, Hq, S, head_dim)
         self.shape_kv = (B, Hkv, S, head_dim)
         mk = lambda shp: torch.empty(shp, dtype=torch.bfloat16, device=self.device)  # noqa: E731
         self.q, self.k, self.v, self.o = mk(self.shape_q), mk(self.shape_kv), mk(self.shape_kv), mk(self.shape_q)
+        self.k_rot = mk(self.shape_kv) if rope == "prepass_k" else None
         self.causal, self.rope = causal, rope
-        self.cos, self.sin = kernels.rope_cache(S, head_dim, theta, device=self.device) if rope else (None, None)
+        self.cos, self.sin = kernels.rope_cache(S, head_dim, theta, device=self.device) if rope != "none" \
+            else (None, None)
+
+    def launches_per_step(self) -> int:
+        return 2 if self.rope == "prepass_k" else 1
 
     def h2d_bytes(self) -> int:
         return (self.q.numel() + self.k.numel() + self.v.numel()) * 2
@@ -31,8 +50,13 @@ class PrefillSession:
         return self.o.numel() * 2
 
     def run_device(self) -> torch.Tensor:
-        return kernels.prefill(self.q, self.k, self.v, self.cos, self.sin, causal=self.causal, rope_q=self.rope,
-                               rope_k=self.rope, out=self.o)
+        if self.rope == "prepass_k":
+            kernels.rope(self.k, self.cos, self.sin, out=self.k_rot)
+            return kernels.prefill(self.q, self.k_rot, self.v, self.cos, self.sin, causal=self.causal, rope_q=True,
+                                   out=self.o)
+        fused = self.rope == "fused"
+        return kernels.prefill(self.q, self.k, self.v, self.cos, self.sin, causal=self.causal, rope_q=fused,
+                               rope_k=fused, out=self.o)
 
     def run_host(self, q_h: torch.Tensor, k_h: torch.Tensor, v_h: torch.Tensor, out_h: torch.Tensor) -> torch.Tensor:
         """q_h/k_h/v_h/out_h: bf16 CPU tensors (pin them for asynchronous copies)."""
