@@ -17,6 +17,8 @@
 #include "common.cuh"
 #include "gqa_internal.h"
 
+#include <cstdlib>
+
 namespace gqa {
 namespace decode {
 
@@ -24,7 +26,7 @@ constexpr int kD = 128;
 constexpr int kG = 4;
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kDefaultSplit = 1024;
+constexpr int kDefaultSplit = 2048;
 
 struct Params {
   const uint16_t* q;
@@ -231,6 +233,16 @@ inline int effective_split(int max_len, int split_len) {
   return kDefaultSplit;
 }
 
+// The tcgen05 split-KV kernel (decode_sm100.cu) is the default; GQA_DECODE_CUDA_CORES=1
+// selects the CUDA-core kernel above (kept as a cross-check of the tensor-core path).
+inline bool use_tensor_core_decode() {
+  static const bool tc = [] {
+    const char* e = getenv("GQA_DECODE_CUDA_CORES");
+    return !(e && e[0] == '1');
+  }();
+  return tc;
+}
+
 }  // namespace decode
 }  // namespace gqa
 
@@ -287,6 +299,9 @@ extern "C" int gqa_decode_bf16(const void* q, const void* kcache, const void* vc
   p.split_len = sl;
   p.flags = flags;
   p.scale_log2 = scale * 1.4426950408889634f;
+  if (use_tensor_core_decode())
+    return launch_decode_tc(q, kcache, vcache, lens, q_pos, cos, sin, o, ws, B, max_len, Hq, Hkv, kv_head_begin,
+                            kv_head_count, sl, ns, scale, flags, stream);
   decode_split_kernel<<<dim3(ns, kv_head_count, B), kThreads, 0, stream>>>(p);
   if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
   decode_combine_kernel<<<dim3(kv_head_count * kG, B), kD, 0, stream>>>(p);

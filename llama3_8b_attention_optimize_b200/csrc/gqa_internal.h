@@ -35,4 +35,9 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
                    cudaStream_t stream, long long* trace = nullptr, int trace_block = -1);
 
+int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
+                     const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,
+                     int kv_begin, int kv_count, int split_len, int n_splits, float scale, int flags,
+                     cudaStream_t stream);
+
 }  // namespace gqa

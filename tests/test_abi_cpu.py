@@ -62,7 +62,7 @@ def test_host_validation_rejects_bad_arguments(lib):
     assert lib.gqa_prefill_bf16(mis, fake, fake, fake, None, None, 1, 128, 32, 8, 128, 0, 8, 0.1, 1, None) == \
         E.GQA_ERR_MISALIGNED
     # decode: workspace sizing and checks
-    assert lib.gqa_decode_workspace_size(64, 32, 32768, 0) == 64 * 32 * 32 * 130 * 4
+    assert lib.gqa_decode_workspace_size(64, 32, 32768, 0) == 64 * 32 * 16 * 130 * 4
     assert lib.gqa_decode_workspace_size(0, 32, 1, 0) == 0
     assert lib.gqa_decode_bf16(fake, fake, fake, fake, None, None, None, fake, None, 0, 2, 64, 32, 8, 128, 0, 8, 0,
                                0.1, 0, None) == E.GQA_ERR_WORKSPACE

@@ -99,3 +99,27 @@ def test_decode_c5_config_sampled():
     out2 = kernels.decode(q, kc, vc, lens, split_len=4096)
     d = (out.float() - out2.float()).abs()
     assert d.max().item() <= 2e-2 and d.mean().item() <= 1e-4
+
+
+@pytest.mark.parametrize("split", [0, 64, 384])
+def test_decode_ignores_non_finite_cache_past_lens(split):
+    """Cache rows at or past lens[b] may hold anything (NaN, inf): they must not reach the output."""
+    B, Hq, Hkv, Lmax = 4, 32, 8, 1000
+    q = randn_bf16((B, Hq, 128), 71)
+    kc = randn_bf16((B, Hkv, Lmax, 128), 72)
+    vc = randn_bf16((B, Hkv, Lmax, 128), 73)
+    lens_np = np.array([1000, 1, 129, 0], dtype=np.int32)
+    lens = torch.from_numpy(lens_np).cuda()
+    clean = kernels.decode(q, kc, vc, lens, split_len=split)
+    kp, vp = kc.clone(), vc.clone()
+    for b, L in enumerate(lens_np):
+        kp[b, :, L:] = float("nan")
+        vp[b, :, L:] = float("inf") if b % 2 else float("nan")
+    dirty = kernels.decode(q, kp, vp, lens, split_len=split)
+    kernels.device_check()
+    assert torch.equal(clean, dirty)
+    assert torch.isfinite(dirty.float()).all()
+    assert (dirty[3].float() == 0).all()  # an empty sequence gives zeros
+    bs = np.repeat(np.arange(3), Hq)
+    hs = np.tile(np.arange(Hq), 3)
+    _check(dirty, _reference(q, kc, vc, lens_np, bs, hs), bs, hs)
