@@ -69,6 +69,7 @@ class ClockSampler:
         self.idx = gpu_index
         self.proc = None
         self.lines = []
+        self.t0, self.t1 = None, None
 
     def __enter__(self):
         try:
@@ -77,13 +78,18 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(0.5)  # nvidia-smi is sampling before the timed region starts
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def window(self, t0: float, t1: float):
+        """Keep only the samples taken while the timed region ran."""
+        self.t0, self.t1 = t0, t1
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -96,7 +102,9 @@ class ClockSampler:
 
     def summary(self):
         rows = []
-        for ln in self.lines:
+        for t, ln in self.lines:
+            if self.t0 is not None and not (self.t0 <= t <= self.t1 + 0.15):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -224,7 +232,9 @@ def run_ours(args, world, rank, local):
     kernels.device_check(dev)
     flops_rank = causal_flops(B, hq, S_PREFILL, D)
     with ClockSampler(local) as clk:
+        t_a = time.monotonic()
         ms = time_loop(sess.run_device, args.steps, world, stream)
+        clk.window(t_a, time.monotonic())
     kernels.device_check(dev)
     ms_step = ms / args.steps
     flops_total = causal_flops(B, HQ, S_PREFILL, D)
@@ -280,9 +290,9 @@ def run_ours(args, world, rank, local):
         return 0
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        dt, fl, cores = cpu_reference_sample(2, S_PREFILL)
+        dt, fl, cores = cpu_reference_sample(24, S_PREFILL)
         cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-               "sample": "2 query heads (kv head 0, batch element 0) of the seq-8192 workload, NumPy fp32 "
+               "sample": "24 query heads (kv head 0, batch element 0) of the seq-8192 workload, NumPy fp32 "
                          "(CPU_Baseline gqa_attention_cpu restated), %.1f s" % dt}
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -343,7 +353,7 @@ def main():
     ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
                     help="run a small case for ncu captures instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -146,6 +146,43 @@ int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const void* vcach
                             int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
                             float scale, int flags, gqa_stream_t stream);
 
+/* ---------------------------------------------------------------- projections
+ * The full layer's linear maps (golden run_full_attention,
+ * llama3_attention_golden_model.py:149-151 and :193-194): y = x W^T with W in the
+ * HF [out][in] layout, bf16 operands, fp32 accumulation, one round-to-nearest-even
+ * to bf16 -- or, with GQA_GEMM_OUT_F32, the fp32 sums (row-parallel partials that
+ * are all-reduced before the rounding).  Row strides (elements) must keep rows
+ * 16-byte aligned.                                                              */
+#define GQA_GEMM_OUT_F32 1
+
+/* c[M][ldc] = a[M][lda] . w[N][ldw]^T over the first K columns.
+ * Replaces `hidden_states @ q_proj.T` etc. (:149-151, :194).                   */
+int gqa_gemm_bf16(const void* a, const void* w, void* c, int M, int N, int K, int lda, int ldw, int ldc, int flags,
+                  gqa_stream_t stream);
+
+/* Fused q/k/v projection, one launch: h [B][S][hidden]; wq [Hq*128][hidden],
+ * wk / wv [Hkv*128][hidden]; outputs head-major q [B][Hq][S][128], k / v
+ * [B][Hkv][S][128] (the .view().transpose(0,1) of :153-155).  GQA_FLAG_ROPE_Q /
+ * GQA_FLAG_ROPE_K rotate q / k at positions pos0 + s after the bf16 rounding, as
+ * to_bf16(apply_rope(to_bf16(h @ W^T))) (:149-164); cos/sin hold >= pos0 + S rows.
+ * B > 1 needs S % 128 == 0.  For a kv-head shard pass the weight rows of the
+ * shard's heads (wq + 512*g0*hidden, wk/wv + 128*g0*hidden).                    */
+int gqa_qkv_proj_bf16(const void* h, const void* wq, const void* wk, const void* wv, void* q, void* k, void* v,
+                      const void* cos, const void* sin, int B, int S, int hidden, int Hq, int Hkv, int head_dim,
+                      int pos0, int flags, gqa_stream_t stream);
+
+/* o_proj from the head-major attention output attn [B][Hq][S][128]:
+ * out[B*S][N] = concat_h(attn[:, h]) . wo[N][ldw]^T over columns [0, Hq*128) of
+ * wo (the transpose(0,1).view(S,-1) of :193 is folded into the loads).  A shard
+ * owning q heads [h0, h0+Hq) passes wo + h0*128 with ldw = the full width and
+ * GQA_GEMM_OUT_F32; the partials are summed across shards (all-reduce) and
+ * rounded with gqa_cast_f32_bf16.  B > 1 needs S % 128 == 0.                   */
+int gqa_o_proj_bf16(const void* attn, const void* wo, void* out, int B, int S, int Hq, int head_dim, int N, int ldw,
+                    int flags, gqa_stream_t stream);
+
+/* dst[i] = bf16_rne(src[i]) for n fp32 values (src 16-byte aligned, dst 8-byte). */
+int gqa_cast_f32_bf16(const void* src, void* dst, long long n, gqa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,7 @@ GQA_FLAG_CAUSAL = 1
 GQA_FLAG_ROPE_Q = 2
 GQA_FLAG_ROPE_K = 4
 GQA_MASK_NEG_INF_BF16 = 0xFF80
+GQA_GEMM_OUT_F32 = 1
 
 # (name, restype, argtypes) for every symbol include/gqa_b200.h declares.
 _vp, _i, _f, _d, _ll, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_double, ctypes.c_longlong, ctypes.c_size_t
@@ -46,6 +47,10 @@ SIGNATURES = {
     "gqa_decode_noalloc_scratch_bytes": (_sz, []),
     "gqa_decode_bf16_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _i,
                                      _vp]),
+    "gqa_gemm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gqa_qkv_proj_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gqa_o_proj_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gqa_cast_f32_bf16": (_i, [_vp, _vp, _ll, _vp]),
 }
 
 

@@ -40,6 +40,31 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long dim0, long l
   return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_UNSUPPORTED;
 }
 
+int make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const long long dims[4],
+                 const long long strides[3], const int box[4]) {
+  std::call_once(g_encode_once, resolve_encode);
+  if (!g_encode) return GQA_ERR_NO_DEVICE;
+  if (elem_bytes != 2 && elem_bytes != 4) return GQA_ERR_UNSUPPORTED;
+  if (box[0] * elem_bytes > 128 || (box[0] * elem_bytes) % 16) return GQA_ERR_UNSUPPORTED;
+  cuuint64_t gdim[4];
+  cuuint64_t gstride[3];
+  cuuint32_t bx[4], estride[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 4; ++i) {
+    if (dims[i] <= 0 || box[i] <= 0 || box[i] > 256) return GQA_ERR_UNSUPPORTED;
+    gdim[i] = static_cast<cuuint64_t>(dims[i]);
+    bx[i] = static_cast<cuuint32_t>(box[i]);
+  }
+  for (int i = 0; i < 3; ++i) {
+    if (strides[i] <= 0 || strides[i] % 16) return GQA_ERR_MISALIGNED;
+    gstride[i] = static_cast<cuuint64_t>(strides[i]);
+  }
+  CUresult r = g_encode(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                        const_cast<void*>(base), gdim, gstride, bx, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_UNSUPPORTED;
+}
+
 }  // namespace gqa
 
 using namespace gqa;

@@ -18,6 +18,11 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long dim0, long long dim1, long long dim2, int box0,
                       int box1, int box2);
 
+// Encode a 4-D tensor map (bf16 or fp32 elements) with 128-byte swizzle: dims are
+// innermost first, strides (bytes) belong to dims 1..3, box[0] * elem_bytes <= 128.
+int make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const long long dims[4],
+                 const long long strides[3], const int box[4]);
+
 // Set cudaFuncAttributeMaxDynamicSharedMemorySize once per device for `func`.
 template <typename F>
 int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {

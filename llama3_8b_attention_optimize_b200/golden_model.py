@@ -13,7 +13,7 @@ function                 reference                                    computed b
 ``build_rope_cache``     :124-130                                     gqa_rope_cache_bf16
 ``rotate_half``          :133-135                                     torch (index shuffle)
 ``apply_rope``           :138-139 (+ the to_bf16 at :163-164)         gqa_rope_bf16
-``run_full_attention``   :144-197 (all stage dumps)                   projections + stage kernels
+``run_full_attention``   :144-197 (all stage dumps)                   tcgen05 GEMMs + stage kernels
 ``run_attention_core``   :157-190 without the projections             stage kernels / fused kernel
 ``save_dump``            :214-246 (full/ and fpga_slice/ .npy files)  host write
 =======================  ===========================================  ==========================
@@ -96,11 +96,6 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return _back(y, x)
 
 
-def _project(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    # bf16(h @ w^T) with fp32 accumulation (reference :149-151, :194)
-    return torch.matmul(h, w.t())
-
-
 def run_attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
                        debug: bool = True, theta: float = ROPE_THETA) -> dict:
     """Stages q/k RoPE -> scores -> mask -> softmax -> PV for q [Hq,S,d], k/v [Hkv,S,d]
@@ -130,19 +125,17 @@ def run_full_attention(hidden_states: torch.Tensor, q_proj: torch.Tensor, k_proj
     """Full attention layer with every stage dump (reference :144-197).
 
     hidden_states [S, 4096]; q_proj [4096,4096], k_proj/v_proj [1024,4096],
-    o_proj [4096,4096] (HF [out, in] layout), all bf16 values.
+    o_proj [4096,4096] (HF [out, in] layout), all bf16 values.  The projections are
+    the tcgen05 GEMM: one fused launch writes q/k/v head-major (:149-155) and o_proj
+    reads the head-major attention output directly (:193-194).
     """
     dev = hidden_states.device if hidden_states.is_cuda else _dev()
     h = _to_gpu_bf16(hidden_states, dev)
     wq, wk, wv, wo = (_to_gpu_bf16(w, dev) for w in (q_proj, k_proj, v_proj, o_proj))
-    S = h.shape[0]
-    nq, nkv = wq.shape[0] // HEAD_DIM, wk.shape[0] // HEAD_DIM
-    q = _project(h, wq).view(S, nq, HEAD_DIM).transpose(0, 1).contiguous()
-    k = _project(h, wk).view(S, nkv, HEAD_DIM).transpose(0, 1).contiguous()
-    v = _project(h, wv).view(S, nkv, HEAD_DIM).transpose(0, 1).contiguous()
+    q, k, v = kernels.qkv_proj(h, wq, wk, wv, head_dim=HEAD_DIM)
     dump = run_attention_core(q, k, v, debug=debug)
-    attn = dump["attn_out_per_head"].to(device=dev, dtype=torch.bfloat16).transpose(0, 1).contiguous().view(S, -1)
-    dump["final_output"] = _back(_project(attn, wo), hidden_states)
+    attn = dump["attn_out_per_head"].to(device=dev, dtype=torch.bfloat16).contiguous()
+    dump["final_output"] = kernels.o_proj(attn, wo)
     return {key: _back(val, hidden_states) for key, val in dump.items()}
 
 

@@ -11,7 +11,7 @@ import math
 import torch
 
 from . import _lib
-from ._lib import GQA_FLAG_CAUSAL, GQA_FLAG_ROPE_K, GQA_FLAG_ROPE_Q, GqaError, check
+from ._lib import GQA_FLAG_CAUSAL, GQA_FLAG_ROPE_K, GQA_FLAG_ROPE_Q, GQA_GEMM_OUT_F32, GqaError, check
 
 ROPE_THETA = 500000.0
 HEAD_DIM = 128
@@ -211,6 +211,93 @@ def decode(q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, lens: to
                                       B, Lmax, Hq, Hkv, d, kb, kc, split_len,
                                       default_scale(d) if scale is None else float(scale), flags, _stream(q.device)),
           "gqa_decode_bf16")
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, out_f32: bool = False,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(x @ w^T) (or the fp32 sums with ``out_f32``) for x [..., K], w [N, K] in the
+    HF [out, in] layout (golden projections, llama3_attention_golden_model.py:149-151, :194)."""
+    _need(x, "x")
+    _need(w, "w")
+    K = x.shape[-1]
+    if w.dim() != 2 or w.shape[1] != K:
+        raise ValueError("w must be [N, K] with K = x.shape[-1]")
+    N, M = w.shape[0], x.numel() // K
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    out = torch.empty(*x.shape[:-1], N, dtype=odt, device=x.device) if out is None else out
+    _need(out, "out", odt)
+    if out.numel() != M * N:
+        raise ValueError("out has the wrong size")
+    check(_lib.load().gqa_gemm_bf16(_ptr(x), _ptr(w), _ptr(out), M, N, K, K, K, N,
+                                    GQA_GEMM_OUT_F32 if out_f32 else 0, _stream(x.device)), "gqa_gemm_bf16")
+    return out
+
+
+def qkv_proj(h: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor,
+             cos: torch.Tensor | None = None, sin: torch.Tensor | None = None, *, rope_q: bool = False,
+             rope_k: bool = False, pos0: int = 0, head_dim: int = HEAD_DIM,
+             out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None):
+    """Fused q/k/v projection (one launch): h [S, hidden] or [B, S, hidden] -> head-major
+    q [B?, Hq, S, 128], k/v [B?, Hkv, S, 128] = bf16(h @ W^T) viewed per head
+    (golden :149-155); q / k rotated at positions pos0 + s when rope_q / rope_k (:162-164)."""
+    for t, n in ((h, "h"), (wq, "wq"), (wk, "wk"), (wv, "wv")):
+        _need(t, n)
+    batched = h.dim() == 3
+    B, S, hidden = (h.shape if batched else (1, *h.shape))
+    Hq, Hkv = wq.shape[0] // head_dim, wk.shape[0] // head_dim
+    if wq.shape != (Hq * head_dim, hidden) or wk.shape != (Hkv * head_dim, hidden) or wv.shape != wk.shape:
+        raise ValueError("weights must be [H*head_dim, hidden]")
+    lead = (B,) if batched else ()
+    if out is None:
+        q = torch.empty(*lead, Hq, S, head_dim, dtype=torch.bfloat16, device=h.device)
+        k = torch.empty(*lead, Hkv, S, head_dim, dtype=torch.bfloat16, device=h.device)
+        v = torch.empty_like(k)
+    else:
+        q, k, v = out
+    flags = (GQA_FLAG_ROPE_Q if rope_q else 0) | (GQA_FLAG_ROPE_K if rope_k else 0)
+    if flags:
+        if cos is None or sin is None:
+            raise ValueError("rope needs cos/sin tables")
+        _need(cos, "cos")
+        _need(sin, "sin")
+        if cos.shape[0] < pos0 + S:
+            raise ValueError("rope table too short")
+    cp = _ptr(cos) if flags else None
+    sp = _ptr(sin) if flags else None
+    check(_lib.load().gqa_qkv_proj_bf16(_ptr(h), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(q), _ptr(k), _ptr(v), cp, sp,
+                                        B, S, hidden, Hq, Hkv, head_dim, pos0, flags, _stream(h.device)),
+          "gqa_qkv_proj_bf16")
+    return q, k, v
+
+
+def o_proj(attn: torch.Tensor, wo: torch.Tensor, *, head_begin: int = 0, out_f32: bool = False,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """o_proj straight from the head-major attention output attn [B?, H, S, 128]:
+    out [B?, S, N] = concat_h(attn) @ wo[:, head_begin*128 : (head_begin+H)*128]^T (golden :193-194)."""
+    _need(attn, "attn")
+    _need(wo, "wo")
+    a4 = _bhsd(attn, "attn")
+    B, H, S, d = a4.shape
+    N, width = wo.shape
+    if (head_begin + H) * d > width:
+        raise ValueError("wo has fewer input columns than the heads need")
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    shape = (B, S, N) if attn.dim() == 4 else (S, N)
+    out = torch.empty(shape, dtype=odt, device=attn.device) if out is None else out
+    _need(out, "out", odt)
+    w_ptr = _ptr(wo) + head_begin * d * wo.element_size()
+    check(_lib.load().gqa_o_proj_bf16(_ptr(attn), w_ptr, _ptr(out), B, S, H, d, N, width,
+                                      GQA_GEMM_OUT_F32 if out_f32 else 0, _stream(attn.device)), "gqa_o_proj_bf16")
+    return out
+
+
+def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Round an fp32 tensor to bf16 (RNE), e.g. all-reduced o_proj partials."""
+    _need(x, "x", torch.float32)
+    out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    _need(out, "out")
+    check(_lib.load().gqa_cast_f32_bf16(_ptr(x), _ptr(out), x.numel(), _stream(x.device)), "gqa_cast_f32_bf16")
     return out
 
 

@@ -76,6 +76,22 @@ def test_host_validation_rejects_bad_arguments(lib):
     assert lib.gqa_scores_bf16(fake, fake, fake, 1, 6, 4, 8, 128, 0.1, None) == E.GQA_ERR_INVALID_ARGUMENT
     assert lib.gqa_softmax_bf16(fake, fake, 0, 8, None) == E.GQA_ERR_INVALID_ARGUMENT
     assert lib.gqa_pv_bf16(fake, fake, None, 1, 4, 1, 8, 128, None) == E.GQA_ERR_INVALID_ARGUMENT
+    # projections
+    assert lib.gqa_gemm_bf16(None, fake, fake, 64, 64, 64, 64, 64, 64, 0, None) == E.GQA_ERR_INVALID_ARGUMENT
+    assert lib.gqa_gemm_bf16(fake, fake, fake, 64, 64, 64, 32, 64, 64, 0, None) == E.GQA_ERR_INVALID_ARGUMENT  # lda < K
+    assert lib.gqa_gemm_bf16(fake, fake, fake, 64, 64, 64, 64, 64, 64, 8, None) == E.GQA_ERR_INVALID_ARGUMENT  # flag
+    assert lib.gqa_gemm_bf16(fake, fake, fake, 64, 64, 100, 100, 100, 64, 0, None) == E.GQA_ERR_MISALIGNED
+    assert lib.gqa_gemm_bf16(mis, fake, fake, 64, 64, 64, 64, 64, 64, 0, None) == E.GQA_ERR_MISALIGNED
+    assert lib.gqa_qkv_proj_bf16(fake, fake, fake, fake, fake, fake, fake, None, None, 1, 64, 4096, 32, 8, 128, 0,
+                                 E.GQA_FLAG_ROPE_Q, None) == E.GQA_ERR_INVALID_ARGUMENT  # rope without tables
+    assert lib.gqa_qkv_proj_bf16(fake, fake, fake, fake, fake, fake, fake, None, None, 1, 64, 4096, 32, 8, 64, 0,
+                                 0, None) == E.GQA_ERR_UNSUPPORTED  # head_dim
+    assert lib.gqa_qkv_proj_bf16(fake, fake, fake, fake, fake, fake, fake, None, None, 2, 100, 4096, 32, 8, 128, 0,
+                                 0, None) == E.GQA_ERR_UNSUPPORTED  # batched S not a multiple of 128
+    assert lib.gqa_o_proj_bf16(fake, fake, fake, 1, 64, 32, 128, 4096, 1024, 0, None) == \
+        E.GQA_ERR_INVALID_ARGUMENT  # ldw narrower than the heads
+    assert lib.gqa_cast_f32_bf16(None, fake, 16, None) == E.GQA_ERR_INVALID_ARGUMENT
+    assert lib.gqa_cast_f32_bf16(fake, fake, 0, None) == E.GQA_OK
 
 
 def test_python_wrappers_refuse_cpu_tensors():
