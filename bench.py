@@ -11,7 +11,10 @@ Workload (one step = one launch of the fused kernel over one batch):
   heads [8r/N, 8(r+1)/N) of every sequence (KV-head sharding, no collective), so the
   work per GPU is fixed ("weak" scaling).  Inputs (335 MB per rank) exceed L2.
 Also measured: split-KV decode, batch 64 (64N across ranks), cache lengths
-U[1024, 32768], reported in HBM GB/s under "decode".
+U[1024, 32768], reported in HBM GB/s under "decode"; and one full attention layer
+(seq 4096, hidden 4096: fused q/k/v projection with RoPE, causal core, o_proj, and
+across ranks an fp32 NCCL all-reduce of the row-parallel o_proj partials) in TFLOP/s
+under "full_layer" (total work fixed: strong scaling).
 
 Prints ONE JSON line on rank 0.
 """
@@ -33,6 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 HQ, HKV, D, S_PREFILL, B_PER_GPU = 32, 8, 128, 8192, 4
+LAYER_S = 4096
 DEC_B, DEC_LMAX = 64, 32768
 METRIC = "GQA causal prefill TFLOP/s (seq 8192) at 1/2/4/8 B200; decode HBM GB/s"
 
@@ -143,11 +147,11 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -275,6 +279,10 @@ def run_ours(args, world, rank, local):
     dec_gbs = dec_bytes_total / (ms_dec * 1e-3) / 1e9
     del kc, vc
 
+    # ---- full attention layer (S=4096, hidden 4096): q/k/v projection with RoPE in the
+    # epilogue, causal core, o_proj (+ fp32 all-reduce across ranks): strong scaling
+    layer = run_layer(args, world, rank, dev, stream)
+
     hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
     prof = load_profile_traffic()
     achieved = flops_rank / (ms_step * 1e-3) / 1e12
@@ -311,11 +319,50 @@ def run_ours(args, world, rank, local):
         "decode": {"metric": "split-KV GQA decode HBM GB/s", "value": dec_gbs, "unit": "GB/s", "ms_per_step": ms_dec,
                    "config": {"batch": dB, "max_len": DEC_LMAX, "lens": "U[1024,32768] seed 99",
                               "kv_heads_per_gpu": hkv}, "roofline": dec_roof, "gpu_launches": 2 * dsteps},
+        "full_layer": layer,
     }
+    lt = layer["achieved_per_gpu"]
+    layer["roofline"] = {"bound": "tensor", "achieved": lt, "peak": tc_peak, "unit": "TFLOP/s", "frac": lt / tc_peak}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return 0
+
+
+def run_layer(args, world, rank, dev, stream) -> dict:
+    from llama3_8b_attention_optimize_b200 import kernels
+    from llama3_8b_attention_optimize_b200.layer import FullLayerSession, reduce_partials
+
+    ls = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev)
+    g = torch.Generator(device=dev).manual_seed(4242)  # identical weights and input on every rank
+    wq = (torch.randn(4096, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wk = (torch.randn(1024, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wv = (torch.randn(1024, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wo = (torch.randn(4096, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ls.set_weights(wq, wk, wv, wo)
+    ls.h.copy_(torch.randn(ls.h.shape, generator=g, device=dev))
+    del wq, wk, wv, wo
+    for _ in range(args.warmup):
+        ls.run_device()
+    kernels.device_check(dev)
+    lsteps = max(args.steps // 4, 10)
+    ms = time_loop(ls.run_device, lsteps, world, stream) / lsteps
+    kernels.device_check(dev)
+    fl = ls.flops()
+    out = {"metric": "attention layer TFLOP/s (q/k/v proj + RoPE + causal GQA core + o_proj)", "unit": "TFLOP/s",
+           "value": fl["total"] / (ms * 1e-3) / 1e12, "ms_per_step": ms, "steps": lsteps, "scaling": "strong",
+           "achieved_per_gpu": fl["total"] / world / (ms * 1e-3) / 1e12,
+           "config": {"seq_len": LAYER_S, "batch": 1, "hidden": 4096, "q_heads": HQ, "kv_heads": HKV,
+                      "parallelism": f"kv_head_shard{world} (column-parallel qkv, row-parallel o_proj)",
+                      "flops": fl},
+           "gpu_launches": lsteps * (3 if world == 1 else 4)}
+    if world > 1:
+        ar = time_loop(lambda: reduce_partials(ls.partial, world), lsteps, world, stream) / lsteps
+        nbytes = ls.partial.numel() * 4
+        out["all_reduce"] = {"ms": ar, "bytes": nbytes, "dtype": "fp32",
+                             "bus_gbs": nbytes * 2 * (world - 1) / world / (ar * 1e-3) / 1e9}
+    del ls
+    return out
 
 
 def run_profile_case(args):

@@ -205,3 +205,30 @@ def test_c4_projection_shapes_sampled_rows():
         _check_bf16(t[:, rows].transpose(0, 1), _reshape(_exact(h, w, rows), len(rows), H, 128))
     flat = attn.transpose(0, 1).contiguous().view(S, 4096)
     _check_bf16(o[rows], _exact(flat, wo, rows))
+
+
+def test_layer_session_matches_facade_and_shards_sum():
+    """FullLayerSession (RoPE in the projection epilogue) == run_full_attention(debug=False)
+    bit for bit; two row-parallel shards summed in fp32 agree to the GEMM bound."""
+    from llama3_8b_attention_optimize_b200.layer import FullLayerSession
+    S = 256
+    h = randn_bf16((1, S, 4096), 61)
+    ws = [randn_bf16(shp, 62 + i, scale=0.02) for i, shp in enumerate(((4096, 4096), (1024, 4096), (1024, 4096),
+                                                                       (4096, 4096)))]
+    sess = FullLayerSession(S)
+    sess.set_weights(*ws)
+    sess.h.copy_(h)
+    out = sess.run_device().clone()
+    dump = golden_model.run_full_attention(h[0], *ws, debug=False)
+    kernels.device_check()
+    assert torch.equal(out[0], dump["final_output"].to(torch.bfloat16))
+    parts = []
+    for r in range(2):
+        sh = FullLayerSession(S, rank=r, world=2)
+        sh.set_weights(*ws)
+        sh.h.copy_(h)
+        parts.append(sh.run_partial().clone())
+    total = kernels.cast_bf16(parts[0] + parts[1])
+    kernels.device_check()
+    attn = sess.attn[0].transpose(0, 1).contiguous().view(S, -1)
+    _check_bf16(total[0], _exact(attn, ws[3]))
