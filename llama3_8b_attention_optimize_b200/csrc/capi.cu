@@ -88,12 +88,16 @@ extern "C" int gqa_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   if (site) *site = 0;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return GQA_ERR_CUDA;
-  int flag = 0;
-  if (cudaMemcpyFromSymbol(&flag, g_gqa_dev_error, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
-  if (flag == 0) return GQA_OK;
-  const int zero = 0;
-  if (cudaMemcpyToSymbol(g_gqa_dev_error, &zero, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
-  if (site) *site = flag;
+  int (*const readers[])(bool) = {error_flag_stages, error_flag_prefill, error_flag_decode, error_flag_decode_tc,
+                                   error_flag_gemm};
+  int first = 0;
+  for (auto rd : readers) {  // read and clear every file's word; report the first set one
+    const int v = rd(true);
+    if (v < 0) return GQA_ERR_CUDA;
+    if (first == 0) first = v;
+  }
+  if (first == 0) return GQA_OK;
+  if (site) *site = first;
   return GQA_ERR_DEVICE_TIMEOUT;
 }
 

@@ -16,9 +16,24 @@
 
 namespace gqa {
 
-// Sticky device error word: 0 = OK, else (site code). Read and cleared by
-// gqa_device_check() on the host.
-extern __device__ int g_gqa_dev_error;
+// Sticky device error word of this translation unit: 0 = OK, else the site code of
+// the first wait that gave up.  Every .cu file is its own device module (no
+// relocatable device code, so that setmaxnreg register reallocation stays in
+// force), so each keeps its own word; GQA_ERROR_FLAG_ACCESSOR gives the host a
+// reader per file, and gqa_device_check() polls them all.
+static __device__ int g_gqa_dev_error = 0;
+
+// Host reader of this file's error word (optionally clearing it); -1 on a CUDA error.
+#define GQA_ERROR_FLAG_ACCESSOR(fn)                                                      \
+  int fn(bool clear) {                                                                   \
+    int v = 0;                                                                           \
+    if (cudaMemcpyFromSymbol(&v, g_gqa_dev_error, sizeof(int)) != cudaSuccess) return -1; \
+    if (clear && v != 0) {                                                               \
+      const int z = 0;                                                                   \
+      if (cudaMemcpyToSymbol(g_gqa_dev_error, &z, sizeof(int)) != cudaSuccess) return -1; \
+    }                                                                                    \
+    return v;                                                                            \
+  }
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 
@@ -135,9 +150,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Bring the 128-byte line holding `ptr` into L1 (no register result).
+__device__ __forceinline__ void prefetch_l1(const void* ptr) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr));
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Bring a 3-D tile into L2 ahead of its load (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(c0), "r"(c1),
+               "r"(c2)
+               : "memory");
 }
 
 // 3-D tiled load; c0 is the innermost (contiguous) coordinate in elements and
@@ -334,6 +361,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// acc.x += bf16 w[15:0], acc.y += bf16 w[31:16] (exact widening, fp32 round-to-nearest
+// add): the sm_100 mixed-precision add takes the bf16 halves directly, with no unpacking.
+__device__ __forceinline__ void add_bf16x2_to_f32(float2& acc, uint32_t w) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.bf16 %0, lo, %0;\n\t"
+      "add.rn.f32.bf16 %1, hi, %1;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(w));
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }

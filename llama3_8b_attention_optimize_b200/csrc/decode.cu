@@ -380,3 +380,7 @@ extern "C" int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const 
   return gqa_decode_bf16(q, kcache, vcache, lens, q_pos, cos, sin, o, scratch, kNoAllocScratchBytes, B, max_len, Hq,
                          Hkv, head_dim, kv_head_begin, kv_head_count, split_len, scale, flags, stream);
 }
+
+namespace gqa {
+GQA_ERROR_FLAG_ACCESSOR(error_flag_decode)
+}  // namespace gqa

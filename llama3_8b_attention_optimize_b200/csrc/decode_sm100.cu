@@ -502,3 +502,7 @@ int launch_decode_tc(const void* q, const void* kcache, const void* vcache, cons
 }
 
 }  // namespace gqa
+
+namespace gqa {
+GQA_ERROR_FLAG_ACCESSOR(error_flag_decode_tc)
+}  // namespace gqa

@@ -624,3 +624,7 @@ extern "C" int gqa_cast_f32_bf16(const void* src, void* dst, long long n, gqa_st
                                                                            static_cast<uint16_t*>(dst), n);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
+
+namespace gqa {
+GQA_ERROR_FLAG_ACCESSOR(error_flag_gemm)
+}  // namespace gqa

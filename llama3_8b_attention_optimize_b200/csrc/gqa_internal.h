@@ -36,6 +36,13 @@ int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {
   return GQA_OK;
 }
 
+// Per-file device error words (see GQA_ERROR_FLAG_ACCESSOR): value, optionally cleared.
+int error_flag_stages(bool clear);
+int error_flag_prefill(bool clear);
+int error_flag_decode(bool clear);
+int error_flag_decode_tc(bool clear);
+int error_flag_gemm(bool clear);
+
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
                    cudaStream_t stream, long long* trace = nullptr, int trace_block = -1);

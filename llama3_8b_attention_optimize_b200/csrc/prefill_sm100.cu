@@ -7,10 +7,18 @@
 // core of CPU_Baseline (CPU_Baseline/cpu_baseline/attention.py:60-84), without
 // materialising the S x S score matrix.
 //
-// Work unit (one CTA): batch b, kv head g, a block of 64 query positions.  The CTA
-// holds two 128-row Q tiles; each tile packs the 4 query heads of group g x 32
-// positions (row r = head_in_group*32 + position_offset), so one K/V tile in shared
-// memory serves all 4 heads of the group (GQA by address, no KV duplication).
+// Work unit: batch b, kv head g, a block of 64 query positions, held as two 128-row
+// Q tiles; each tile packs the 4 query heads of group g x 32 positions (row r =
+// head_in_group*32 + position_offset), so one K/V tile in shared memory serves all 4
+// heads of the group (GQA by address, no KV duplication).
+//
+// Persistent CTAs (one per SM) walk the units heaviest-first (causal: most K tiles
+// first) in snake order over the rounds, so each SM gets a balanced share.  Nothing
+// drains between units: the K/V ring and every barrier phase run on across them, the
+// next unit's Q is prefetched into L2 and loaded as soon as the last QK^T of the
+// current unit is done, the softmax threads rotate it before the current unit's
+// epilogue, and its first QK^T overlaps that epilogue (O is normalised from TMEM into
+// the tile's P buffer and written out by TMA).
 //
 // Pipeline: each softmax thread copies its row of S_t (128 keys) from TMEM into
 // registers and releases S_t at once, so the tensor core computes S_t for the next
@@ -21,9 +29,12 @@
 //   warps 0-15 four softmax warpgroups; warpgroup g serves Q tile g/2 and key/dim half
 //              g%2 (thread r owns TMEM lane / row r; the two halves of a row exchange
 //              their partial row max through shared memory)
-//   warp 16    TMA producer (Q tiles, then K0 K1 V0 K2 V1 ... into a 3-stage ring)
+//   warp 16    TMA producer (Q tiles of each unit, then K0 K1 V0 K2 V1 ... into a
+//              3-stage ring)
 //   warp 17    tcgen05.mma issuer (one elected thread) + TMEM allocator
-//   warps 18-19 RoPE of K tiles in shared memory (when FLAG_ROPE_K)
+//   warps 18-19 RoPE of K tiles in shared memory (FLAG_ROPE_K); Q tiles are rotated
+//              by the softmax threads (FLAG_ROPE_Q), the next unit's before the
+//              current unit's epilogue
 // TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 //
 // Online softmax in the log2 domain: p = 2^(s*scale*log2e - m); the running max m is
@@ -52,6 +63,14 @@ constexpr int kWarpProducer = 16;
 constexpr int kWarpMma = 17;
 constexpr int kWarpRope0 = 18;
 constexpr int kThreads = 640;
+// Register split (setmaxnreg): the launch gives every thread kRegsLaunch registers; the
+// helper warpgroup (warps 16-19) gives some back and the four softmax warpgroups take
+// them.  The sum must stay within the launch allocation, or setmaxnreg.inc would wait
+// forever; the host checks the compiled register count before every launch.
+constexpr int kRegsLaunch = 96;
+constexpr int kRegsHelper = 64;
+constexpr int kRegsSoftmax = 104;
+static_assert(4 * 128 * kRegsSoftmax + 128 * kRegsHelper <= kThreads * kRegsLaunch, "register split over budget");
 
 // The 1024-byte-aligned tiles come first; the dynamic shared-memory base is
 // 1024-byte aligned (checked at run time), so no alignment slack is allocated.
@@ -66,17 +85,27 @@ constexpr int kSmemBytes = kOffTmemPtr + 16;
 static_assert(kSmemBytes <= 232448, "shared memory over the per-block limit");
 
 enum : int {
-  B_QFULL = 0,     // [2]  TMA Q landed
-  B_QREADY = 2,    // [2]  Q (rotated) visible to the tensor core, 128 arrivals
-  B_KVFULL = 4,    // [3]  TMA K/V stage landed
-  B_KVEMPTY = 7,   // [3]  MMAs reading the stage completed
-  B_KREADY = 10,   // [4]  K tile j rotated (slot j % 4), 64 arrivals
-  B_SFULL = 14,    // [2]  S_t = Q_t K^T complete
-  B_SFREE = 16,    // [1]  S_0 and S_1 copied to registers (512 arrivals)
-  B_PREADY = 18,   // [1]  P_0 and P_1 in shared memory, O rescaled (512 arrivals)
-  B_PVDONE = 20,   // [2]  O_t += P_t V complete (P_t buffer free)
-  B_DRAIN = 22,    // [1]  every MMA of the CTA complete
+  B_QFULL = 0,     // [2]  TMA Q tile t of the current unit landed
+  B_QREADY = 2,    // [2]  Q tile t (rotated) visible to the tensor core, 256 arrivals
+  B_QEMPTY = 4,    // [1]  last QK^T of the unit complete: the Q tiles may be reloaded
+  B_KVFULL = 5,    // [3]  TMA K/V stage landed
+  B_KVEMPTY = 8,   // [3]  MMAs reading the stage completed
+  B_KREADY = 11,   // [4]  K tile rotated (slot k % 4), 64 arrivals
+  B_SFULL = 15,    // [2]  S_t = Q_t K^T complete
+  B_SFREE = 17,    // [2]  S_t copied to registers (kMmaOrder 0: one barrier for both tiles)
+  B_PREADY = 19,   // [2]  P_t in shared memory, O_t rescaled (kMmaOrder 0: one for both)
+  B_PVDONE = 21,   // [2]  O_t += P_t V complete (P_t buffer free)
+  B_DRAIN = 23,    // [1]  every MMA of the CTA complete
 };
+// Order of the tensor-core work per K tile j:
+//   0: QK0(j+1) QK1(j+1) PV0(j) PV1(j), S/P hand-offs joint for both tiles
+//   1: same order, hand-offs per tile
+//   2: QK0(j+1) PV0(j) QK1(j+1) PV1(j), hand-offs per tile (the tiles' softmax phases
+//      half an iteration apart)
+constexpr int kMmaOrder = 1;
+constexpr int kHandoffThreads = kMmaOrder == 0 ? kSoftmaxThreads : kSoftmaxThreads / 2;
+__device__ __forceinline__ int sfree_bar(int t) { return B_SFREE + (kMmaOrder == 0 ? 0 : t); }
+__device__ __forceinline__ int pready_bar(int t) { return B_PREADY + (kMmaOrder == 0 ? 0 : t); }
 constexpr int kKReadySlots = 4;
 
 // Load order of the K/V ring: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1).  With K
@@ -96,7 +125,7 @@ enum : int {  // error sites reported through g_gqa_dev_error
 };
 
 struct Params {
-  int B, S, Hq, Hkv, kv_begin, kv_count, n_qblocks;
+  int B, S, Hq, Hkv, kv_begin, kv_count, n_qblocks, n_units;
   int flags;
   float scale_log2;
   const uint16_t* cos;  // [>= S][128] bf16 (cat(freqs, freqs) layout)
@@ -202,32 +231,42 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
                      __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
-// One 32-column chunk of S -> 16 packed bf16 pairs of p = 2^(s*scale_log2 - m) at
-// out[base..base+16); acc += the bf16-rounded p.
+// One 32-column chunk of S -> p = 2^(s*scale_log2 - m) as bf16, stored straight into
+// the K-major SW128 P tile (row r, 16-byte chunks c0..c0+3); acc += the bf16-rounded p.
 template <bool kEmulate>
-__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[32], uint32_t (&out)[32], int base, float2 sc2,
-                                          float2 nm2, float2& acc) {
+__device__ __forceinline__ void exp_chunk_store(const uint32_t (&s)[32], uint8_t* ptile, int r, int c0, float2 sc2,
+                                                float2 nm2, float2& acc) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), sc2, nm2);
-    float2 e;
-    if (kEmulate && (i & 3) == 3) {
-      e = exp2_poly2(x);
-    } else {
-      e.x = ex2_approx(x.x);
-      e.y = ex2_approx(x.y);
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * c + e;
+      const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), sc2, nm2);
+      float2 y;
+      if (kEmulate && e == 3) {
+        y = exp2_poly2(x);
+      } else {
+        y.x = ex2_approx(x.x);
+        y.y = ex2_approx(x.y);
+      }
+      w[e] = pack_bf16x2(y.x, y.y);
+      // the row sum uses the bf16 values PV multiplies, so O / l normalises exactly them
+      add_bf16x2_to_f32(acc, w[e]);
     }
-    const uint32_t w = pack_bf16x2(e.x, e.y);
-    out[base + i] = w;
-    // the row sum uses the bf16 values PV multiplies, so O / l normalises exactly them
-    acc = __fadd2_rn(acc, make_float2(bf16_lo(w), bf16_hi(w)));
+    *reinterpret_cast<uint4*>(ptile + sw128_chunk(r, c0 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
+
+struct Unit {
+  int p0, n_kv, zq, zk;
+};
 
 template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Params p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                   const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {  // uniform across the CTA: leave before any barrier
     if (threadIdx.x == 0) record_error(SITE_SMEM_ALIGN);
@@ -239,36 +278,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
 
-  // ---- work unit (heaviest causal blocks first)
-  const int per_qb = p.B * p.kv_count;
-  const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x) / per_qb;
-  const int rem = static_cast<int>(blockIdx.x) % per_qb;
-  const int b = rem / p.kv_count;
-  const int kvh = p.kv_begin + rem % p.kv_count;
-  const int cta_p0 = qb * kPosPerCta;
   const bool causal = (p.flags & GQA_FLAG_CAUSAL) != 0;
   const bool rope_q = (p.flags & GQA_FLAG_ROPE_Q) != 0;
   const bool rope_k = (p.flags & GQA_FLAG_ROPE_K) != 0;
   const int n_kv_all = (p.S + kBN - 1) / kBN;
-  const int n_kv = causal ? min(n_kv_all, (cta_p0 + kPosPerCta - 1) / kBN + 1) : n_kv_all;
-  const int zq = b * p.Hq + kvh * kG;  // first Q/O head row of the group
-  const int zk = b * p.Hkv + kvh;
+  const int n_ctas = static_cast<int>(gridDim.x);
+  const int n_rounds = (p.n_units + n_ctas - 1) / n_ctas;
+  // Unit of round i for this CTA (snake order over the heaviest-first list), -1 if none.
+  auto unit_of = [&](int i) -> int {
+    const int c = (i & 1) ? n_ctas - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+    const int u = i * n_ctas + c;
+    return u < p.n_units ? u : -1;
+  };
+  auto decode = [&](int u) -> Unit {
+    const int per_qb = p.B * p.kv_count;
+    const int qb = p.n_qblocks - 1 - u / per_qb;
+    const int rem = u % per_qb;
+    const int b = rem / p.kv_count;
+    const int kvh = p.kv_begin + rem % p.kv_count;
+    Unit x;
+    x.p0 = qb * kPosPerCta;
+    x.n_kv = causal ? min(n_kv_all, (x.p0 + kPosPerCta - 1) / kBN + 1) : n_kv_all;
+    x.zq = b * p.Hq + kvh * kG;  // first Q/O head row of the group
+    x.zk = b * p.Hkv + kvh;
+    return x;
+  };
 
   if (threadIdx.x == 0) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B_QFULL + t), 1);
       mbar_init(bar(B_QREADY + t), 256);
       mbar_init(bar(B_SFULL + t), 1);
-
       mbar_init(bar(B_PVDONE + t), 1);
     }
+    mbar_init(bar(B_QEMPTY), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(B_KVFULL + s), 1);
       mbar_init(bar(B_KVEMPTY + s), 1);
     }
     for (int k = 0; k < kKReadySlots; ++k) mbar_init(bar(B_KREADY + k), 64);
-    mbar_init(bar(B_SFREE), kSoftmaxThreads);
-    mbar_init(bar(B_PREADY), kSoftmaxThreads);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(B_SFREE + t), kHandoffThreads);
+      mbar_init(bar(B_PREADY + t), kHandoffThreads);
+    }
     mbar_init(bar(B_DRAIN), 1);
     fence_mbar_init();
   }
@@ -291,40 +343,64 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ TMA producer
+    regs_dec<kRegsHelper>();
     if (lane == 0) {
-      for (int t = 0; t < 2; ++t) {
-        const uint32_t dst = sbase + kOffQ + t * kTileBytes;
-        mbar_expect_tx(bar(B_QFULL + t), kTileBytes);
-        tma_load_3d(dst, &tmQ, bar(B_QFULL + t), 0, cta_p0 + t * kRowsPerHead, zq);
-        tma_load_3d(dst + kHalf, &tmQ, bar(B_QFULL + t), 64, cta_p0 + t * kRowsPerHead, zq);
-      }
-      const int nloads = 2 * n_kv;
-      int issued = 0;
       bool ok = true;
-      for (int i = 0; i < nloads; ++i) {
-        const int s = i % kStages, r = i / kStages;
-        if (r > 0) ok = mbar_wait(bar(B_KVEMPTY + s), (r - 1) & 1, SITE_PRODUCER);
-        if (!ok) break;
-        // i -> (tile, K or V) in the K-ahead order
-        const bool is_v = (i == nloads - 1) || (i >= 2 && (i & 1) == 0);
-        const int j = i == 0 ? 0 : (is_v ? (i == nloads - 1 ? n_kv - 1 : (i - 2) >> 1) : (i + 1) >> 1);
-        const void* map = is_v ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
-        const uint32_t dst = sbase + kOffKV + s * kTileBytes;
-        mbar_expect_tx(bar(B_KVFULL + s), kTileBytes);
-        tma_load_3d(dst, map, bar(B_KVFULL + s), 0, j * kBN, zk);
-        tma_load_3d(dst + kHalf, map, bar(B_KVFULL + s), 64, j * kBN, zk);
-        PF_TRACE(0, j, is_v ? 1 : 0);
-        issued = i + 1;
+      uint32_t L = 0;  // K/V loads issued by this CTA (ring position)
+      int uc = 0;      // units started
+      for (int i = 0; ok && i < n_rounds; ++i) {
+        const int u = unit_of(i);
+        if (u < 0) continue;
+        const Unit x = decode(u);
+        // The Q tiles are reused once the previous unit's last QK^T is done.
+        if (uc > 0 && !(ok = mbar_wait(bar(B_QEMPTY), (uc - 1) & 1, SITE_PRODUCER))) break;
+        PF_TRACE(5, uc, 1);
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t dst = sbase + kOffQ + t * kTileBytes;
+          mbar_expect_tx(bar(B_QFULL + t), kTileBytes);
+          tma_load_3d(dst, &tmQ, bar(B_QFULL + t), 0, x.p0 + t * kRowsPerHead, x.zq);
+          tma_load_3d(dst + kHalf, &tmQ, bar(B_QFULL + t), 64, x.p0 + t * kRowsPerHead, x.zq);
+        }
+        const int un = unit_of(i + 1);
+        const int nloads = 2 * x.n_kv;
+        for (int li = 0; li < nloads; ++li) {
+          // Warm L2 with the next unit's Q about eight K tiles before it is loaded (early
+          // enough to hide HBM latency, late enough not to be evicted by the K/V stream).
+          if (un >= 0 && li == max(0, nloads - 16)) {
+            const Unit y = decode(un);
+            for (int t = 0; t < 2; ++t) {
+              tma_prefetch_l2_3d(&tmQ, 0, y.p0 + t * kRowsPerHead, y.zq);
+              tma_prefetch_l2_3d(&tmQ, 64, y.p0 + t * kRowsPerHead, y.zq);
+            }
+          }
+          const int s = static_cast<int>(L % kStages);
+          const uint32_t r = L / kStages;
+          if (r > 0 && !(ok = mbar_wait(bar(B_KVEMPTY + s), (r - 1) & 1u, SITE_PRODUCER))) break;
+          // li -> (tile, K or V) in the K-ahead order
+          const bool is_v = (li == nloads - 1) || (li >= 2 && (li & 1) == 0);
+          const int j = li == 0 ? 0 : (is_v ? (li == nloads - 1 ? x.n_kv - 1 : (li - 2) >> 1) : (li + 1) >> 1);
+          const void* map = is_v ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
+          const uint32_t dst = sbase + kOffKV + s * kTileBytes;
+          mbar_expect_tx(bar(B_KVFULL + s), kTileBytes);
+          tma_load_3d(dst, map, bar(B_KVFULL + s), 0, j * kBN, x.zk);
+          tma_load_3d(dst + kHalf, map, bar(B_KVFULL + s), 64, j * kBN, x.zk);
+          PF_TRACE(0, j, is_v ? 1 : 0);
+          ++L;
+        }
+        ++uc;
       }
       // Drain: every load this thread issued must land before the CTA may exit.
-      for (int i = max(0, issued - kStages); i < issued; ++i)
-        mbar_wait(bar(B_KVFULL + i % kStages), (i / kStages) & 1, SITE_DRAIN);
-      mbar_wait(bar(B_QFULL + 0), 0, SITE_DRAIN);
-      mbar_wait(bar(B_QFULL + 1), 0, SITE_DRAIN);
+      for (uint32_t i = L > static_cast<uint32_t>(kStages) ? L - kStages : 0u; i < L; ++i)
+        mbar_wait(bar(B_KVFULL + static_cast<int>(i % kStages)), (i / kStages) & 1u, SITE_DRAIN);
+      if (uc > 0) {
+        mbar_wait(bar(B_QFULL + 0), (uc - 1) & 1, SITE_DRAIN);
+        mbar_wait(bar(B_QFULL + 1), (uc - 1) & 1, SITE_DRAIN);
+      }
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
+    regs_dec<kRegsHelper>();
     if (lane == 0) {
       constexpr uint32_t kIdQK = idesc_bf16_f32(128, kBN, false);
       constexpr uint32_t kIdPV = idesc_bf16_f32(128, kD, true);
@@ -358,80 +434,169 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_ss_lohi(d, a0 + off, b0 + kk * (2048 / 16), kHi, kIdPV, 1u);
         }
       };
-      auto wait_k = [&](int j) -> bool {  // K tile j landed (and rotated)
-        if (rope_k) return mbar_wait_spin(bar(B_KREADY + j % kKReadySlots), (j / kKReadySlots) & 1, SITE_MMA);
-        const int i = load_idx_k(j);
-        return mbar_wait_spin(bar(B_KVFULL + i % kStages), (i / kStages) & 1, SITE_MMA);
-      };
-      bool ok = mbar_wait_spin(bar(B_QREADY + 0), 0, SITE_MMA) && mbar_wait_spin(bar(B_QREADY + 1), 0, SITE_MMA) &&
-                wait_k(0);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0, 0);
-        umma_commit(bar(B_SFULL + 0));
-        issue_qk(1, 0);
-        umma_commit(bar(B_SFULL + 1));
-        umma_commit(bar(B_KVEMPTY + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        PF_TRACE(1, j, 0);
-        if (j + 1 < n_kv) {
-          // next S as soon as the softmax warps hold S(j) in registers
-          const int sk = load_idx_k(j + 1) % kStages;
-          ok = wait_k(j + 1) && mbar_wait_spin(bar(B_SFREE), j & 1, SITE_MMA);
-          if (!ok) break;
-          PF_TRACE(1, j, 1);
+      bool ok = true;
+      uint32_t L = 0, Gb = 0, Kb = 0;  // ring position, global iteration, K tiles consumed
+      int uc = 0;
+      for (int i = 0; ok && i < n_rounds; ++i) {
+        const int u = unit_of(i);
+        if (u < 0) continue;
+        const int n = decode(u).n_kv;
+        auto wait_k = [&](int j) -> bool {  // K tile j of this unit landed (and rotated)
+          if (rope_k) {
+            const uint32_t kk = Kb + j;
+            return mbar_wait_spin(bar(B_KREADY + kk % kKReadySlots), (kk / kKReadySlots) & 1u, SITE_MMA);
+          }
+          const uint32_t ii = L + load_idx_k(j);
+          return mbar_wait_spin(bar(B_KVFULL + ii % kStages), (ii / kStages) & 1u, SITE_MMA);
+        };
+        // Q of this unit ready, and the S buffers released by the previous unit's softmax
+        ok = mbar_wait_spin(bar(B_QREADY + 0), uc & 1, SITE_MMA) && mbar_wait_spin(bar(B_QREADY + 1), uc & 1, SITE_MMA);
+        PF_TRACE(5, uc, 6);
+        ok = ok && wait_k(0) &&
+             (Gb == 0 || (mbar_wait_spin(bar(sfree_bar(0)), (Gb - 1) & 1u, SITE_MMA) &&
+                          mbar_wait_spin(bar(sfree_bar(1)), (Gb - 1) & 1u, SITE_MMA)));
+        PF_TRACE(5, uc, 7);
+        if (!ok) break;
+        {
+          const int sk = static_cast<int>((L + load_idx_k(0)) % kStages);
           tc_fence_after();
           issue_qk(0, sk);
           umma_commit(bar(B_SFULL + 0));
-          PF_TRACE(1, j, 2);
           issue_qk(1, sk);
           umma_commit(bar(B_SFULL + 1));
           umma_commit(bar(B_KVEMPTY + sk));
-          PF_TRACE(1, j, 3);
+          if (n == 1) umma_commit(bar(B_QEMPTY));
         }
-        const int iv = load_idx_v(j, n_kv), sv = iv % kStages;
-        ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1, SITE_MMA) &&
-             mbar_wait_spin(bar(B_PREADY), j & 1, SITE_MMA);
-        if (!ok) break;
-        PF_TRACE(1, j, 4);
-        tc_fence_after();
-        issue_pv(0, sv, j > 0 ? 1u : 0u);
-        umma_commit(bar(B_PVDONE + 0));
-        PF_TRACE(1, j, 5);
-        PF_TRACE(1, j, 6);
-        tc_fence_after();
-        issue_pv(1, sv, j > 0 ? 1u : 0u);
-        umma_commit(bar(B_PVDONE + 1));
-        umma_commit(bar(B_KVEMPTY + sv));
-        PF_TRACE(1, j, 7);
+        for (int j = 0; ok && j < n; ++j) {
+          const uint32_t g = Gb + j;
+          PF_TRACE(1, g, 0);
+          const int sk = static_cast<int>((L + load_idx_k(j + 1)) % kStages);  // used when j + 1 < n
+          const uint32_t iv = L + load_idx_v(j, n);
+          const int sv = static_cast<int>(iv % kStages);
+          if (kMmaOrder == 2) {
+            // QK0(j+1) PV0(j) QK1(j+1) PV1(j)
+            if (j + 1 < n) {
+              ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(0)), g & 1u, SITE_MMA);
+              if (!ok) break;
+              tc_fence_after();
+              issue_qk(0, sk);
+              umma_commit(bar(B_SFULL + 0));
+            }
+            PF_TRACE(1, g, 1);
+            ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
+                 mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
+            if (!ok) break;
+            PF_TRACE(1, g, 2);
+            tc_fence_after();
+            issue_pv(0, sv, j > 0 ? 1u : 0u);
+            umma_commit(bar(B_PVDONE + 0));
+            PF_TRACE(1, g, 3);
+            if (j + 1 < n) {
+              ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
+              if (!ok) break;
+              tc_fence_after();
+              issue_qk(1, sk);
+              umma_commit(bar(B_SFULL + 1));
+              umma_commit(bar(B_KVEMPTY + sk));
+              if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
+            }
+            PF_TRACE(1, g, 4);
+            ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
+            if (!ok) break;
+            PF_TRACE(1, g, 5);
+            tc_fence_after();
+            issue_pv(1, sv, j > 0 ? 1u : 0u);
+            umma_commit(bar(B_PVDONE + 1));
+            umma_commit(bar(B_KVEMPTY + sv));
+            PF_TRACE(1, g, 7);
+            continue;
+          }
+          if (j + 1 < n) {
+            // next S as soon as the softmax warps hold S(j) in registers
+            ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(0)), g & 1u, SITE_MMA);
+            if (!ok) break;
+            PF_TRACE(1, g, 1);
+            tc_fence_after();
+            issue_qk(0, sk);
+            umma_commit(bar(B_SFULL + 0));
+            PF_TRACE(1, g, 2);
+            if (kMmaOrder == 1) {
+              ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_qk(1, sk);
+            umma_commit(bar(B_SFULL + 1));
+            umma_commit(bar(B_KVEMPTY + sk));
+            if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
+            PF_TRACE(1, g, 3);
+          }
+          ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
+               mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
+          if (!ok) break;
+          PF_TRACE(1, g, 4);
+          tc_fence_after();
+          issue_pv(0, sv, j > 0 ? 1u : 0u);
+          umma_commit(bar(B_PVDONE + 0));
+          PF_TRACE(1, g, 5);
+          if (kMmaOrder == 1) {
+            ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          PF_TRACE(1, g, 6);
+          issue_pv(1, sv, j > 0 ? 1u : 0u);
+          umma_commit(bar(B_PVDONE + 1));
+          umma_commit(bar(B_KVEMPTY + sv));
+          PF_TRACE(1, g, 7);
+        }
+        L += 2 * n;
+        Gb += n;
+        Kb += n;
+        ++uc;
       }
       umma_commit(bar(B_DRAIN));
       mbar_wait(bar(B_DRAIN), 0, SITE_DRAIN);
     }
     __syncwarp();
   } else if (warp >= kWarpRope0) {
-    // ------------------------------------------------------------ RoPE of K tiles
-    if (rope_k) {
-      const int tid = threadIdx.x - kWarpRope0 * 32;  // 0..63
-      for (int j = 0; j < n_kv; ++j) {
-        const int i = load_idx_k(j), s = i % kStages, r = i / kStages;
-        if (!mbar_wait(bar(B_KVFULL + s), r & 1, SITE_ROPEK)) break;
-        if (tid == 0) PF_TRACE(4, j, 0);
-        uint8_t* tile = smem + kOffKV + s * kTileBytes;
+    // ------------------------------------------------------------ RoPE helpers (K tiles)
+    regs_dec<kRegsHelper>();
+    const int tid = threadIdx.x - kWarpRope0 * 32;  // 0..63
+    bool ok = true;
+    uint32_t L = 0, Kb = 0;
+    int uc = 0;
+    for (int i = 0; rope_k && i < n_rounds; ++i) {
+      const int u = unit_of(i);
+      if (u < 0) continue;
+      const Unit x = decode(u);
+      if (tid == 0) PF_TRACE(4, uc, 0);
+      if (rope_k) {
+        for (int j = 0; j < x.n_kv; ++j) {
+          const uint32_t ii = L + load_idx_k(j);
+          const int s = static_cast<int>(ii % kStages);
+          if (ok) ok = mbar_wait(bar(B_KVFULL + s), (ii / kStages) & 1u, SITE_ROPEK);
+          if (ok) {
+            uint8_t* tile = smem + kOffKV + s * kTileBytes;
 #pragma unroll 1
-        for (int rr = tid; rr < kBN; rr += 64) {
-          const int key = j * kBN + rr;
-          if (key < p.S)
-            rope_row_smem(tile, kHalf, rr, p.cos + static_cast<size_t>(key) * kD, p.sin + static_cast<size_t>(key) * kD);
+            for (int rr = tid; rr < kBN; rr += 64) {
+              const int key = j * kBN + rr;
+              if (key < p.S)
+                rope_row_smem(tile, kHalf, rr, p.cos + static_cast<size_t>(key) * kD,
+                              p.sin + static_cast<size_t>(key) * kD);
+            }
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(bar(B_KREADY + (Kb + j) % kKReadySlots));
         }
-        fence_proxy_async_smem();
-        if (tid == 0) PF_TRACE(4, j, 1);
-        mbar_arrive(bar(B_KREADY + j % kKReadySlots));
       }
+      L += 2 * x.n_kv;
+      Kb += x.n_kv;
+      ++uc;
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
+    regs_inc<kRegsSoftmax>();
     const int g = warp >> 2;             // warpgroup 0..3
     const int t = g >> 1;                // Q tile
     const int h = g & 1;                 // keys [64h, 64h+64) of each K tile; O dims [64h, 64h+64)
@@ -439,149 +604,194 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off + colS(t) + 64 * h;
     const uint32_t tO = tmem + lane_off + colO(t) + 64 * h;
-    const int p0 = cta_p0 + t * kRowsPerHead;
-    const int qpos = p0 + (r & (kRowsPerHead - 1));
-    uint8_t* qtile = smem + kOffQ + t * kTileBytes;
     uint8_t* ptile = smem + kOffP + t * kTileBytes;
     float* xchg = reinterpret_cast<float*>(smem + kOffX) + t * 256;  // [half][row]
     const int bar_x = 1 + t;     // named barrier: both halves of tile t (256 threads)
     const int bar_free = 3 + t;  // named barrier: exchange slots may be rewritten
     const float sl2 = p.scale_log2;
+    bool ok = true;
+    bool store_pending = false;  // this thread's TMA store of O may still read P_t
+    uint32_t Gb = 0;             // global iteration of this unit's first K tile
+    int uc = 0;                  // units started
+    // Q tile t of unit y landed: rotate this thread's half of row r in place (each half
+    // rotates 4 of the row's 8 chunk pairs), then release it to the tensor core.
+    auto prepare_q = [&](const Unit& y, int parity, int unit_no) {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_QFULL + t), parity, SITE_SOFTMAX));
+      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, unit_no, 2);
+      const int pos = y.p0 + t * kRowsPerHead + (r & (kRowsPerHead - 1));
+      if (ok && rope_q && pos < p.S)
+        rope_row_smem_part(smem + kOffQ + t * kTileBytes, kHalf, r, p.cos + static_cast<size_t>(pos) * kD,
+                           p.sin + static_cast<size_t>(pos) * kD, 4 * h);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(B_QREADY + t));
+      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, unit_no, 3);
+    };
+    {
+      const int u0 = unit_of(0);
+      if (u0 >= 0) prepare_q(decode(u0), 0, 0);
+    }
 
-    bool ok = mbar_wait(bar(B_QFULL + t), 0, SITE_SOFTMAX);
-    if (ok && rope_q && qpos < p.S)  // each half rotates 4 of the row's 8 chunk pairs
-      rope_row_smem_part(qtile, kHalf, r, p.cos + static_cast<size_t>(qpos) * kD,
-                         p.sin + static_cast<size_t>(qpos) * kD, 4 * h);
-    fence_proxy_async_smem();
-    mbar_arrive(bar(B_QREADY + t));
-    ok = __all_sync(0xffffffffu, ok);
+    // Every warp of the tile runs every iteration of every unit and meets every named
+    // barrier, even after a bounded wait failed (ok == false only skips the work), so
+    // the two halves of a tile can never wait on each other forever.
+    for (int i = 0; i < n_rounds; ++i) {
+      const int u = unit_of(i);
+      if (u < 0) continue;
+      const Unit x = decode(u);
+      const int n_kv = x.n_kv;
+      const int qpos = x.p0 + t * kRowsPerHead + (r & (kRowsPerHead - 1));
+      // last key this row may attend
+      const int lim = causal ? min(qpos, p.S - 1) : p.S - 1;
+      float m_run = -INFINITY, l_run = 0.0f;
+      // the next unit, whose Q this thread rotates before this unit's epilogue
+      int inext = i + 1;
+      while (inext < n_rounds && unit_of(inext) < 0) ++inext;
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t gi = Gb + j;
+        if (j == n_kv - 1 && inext < n_rounds && rope_q) {
+          // pull this row's cos/sin chunks of the next unit into L1 now, so the rotation
+          // between the units does not wait on L2
+          const int pos = decode(unit_of(inext)).p0 + t * kRowsPerHead + (r & (kRowsPerHead - 1));
+          if (pos < p.S) {
+            prefetch_l1(p.cos + static_cast<size_t>(pos) * kD + 32 * h);
+            prefetch_l1(p.sin + static_cast<size_t>(pos) * kD + 32 * h);
+          }
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + t), gi & 1u, SITE_SOFTMAX));
+        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 0);
+        uint32_t s0[32], s1[32];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld32(tS + 0, s0);
+          tmem_ld32(tS + 32, s1);
+          tmem_wait_ld_dep(s0);
+          reg_dep(s1);
+          tc_fence_before();
+          mbar_arrive(bar(sfree_bar(t)));  // S_t may now be overwritten by the next QK^T
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) s0[k] = s1[k] = 0xFF800000u;
+        }
 
-    // last key this row may attend
-    const int lim = causal ? min(qpos, p.S - 1) : p.S - 1;
-    float m_run = -INFINITY, l_run = 0.0f;
-    // Every warp of the tile runs all n_kv iterations and meets every named barrier,
-    // even after a bounded wait failed (ok == false only skips the work), so the two
-    // halves of a tile can never wait on each other forever.
-    for (int j = 0; j < n_kv; ++j) {
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + t), j & 1, SITE_SOFTMAX));
-      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 0);
-      uint32_t s0[32], s1[32];
+        const int rel = lim - j * kBN - 64 * h;  // columns (of this half) > rel are masked
+        if (rel < 63) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            if (k > rel) s0[k] = 0xFF800000u;
+            if (k + 32 > rel) s1[k] = 0xFF800000u;
+          }
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          mx0 = fmax3(mx0, __uint_as_float(s0[k]), __uint_as_float(s0[k + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(s1[k]), __uint_as_float(s1[k + 1]));
+        }
+        // The previous unit's O went out through P_t: the tile writes P_t only after this
+        // barrier, which the storing thread reaches once the stores have read it.
+        if (store_pending) {
+          bulk_wait_read0();
+          store_pending = false;
+        }
+        // row max over both halves: slot [h][r] <-> [1-h][r]
+        named_bar_sync(bar_free, 256);  // everyone has read the previous exchange's slots
+        xchg[h * 128 + r] = fmaxf(mx0, mx1);
+        named_bar_sync(bar_x, 256);
+        const float m_tile = fmaxf(fmaxf(mx0, mx1), xchg[(1 - h) * 128 + r]) * sl2;
+        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 1);
+        const float m_new = fmaxf(m_run, m_tile);
+        const bool need = m_new > m_run + kRescaleLog2;
+        const float m_use = need ? m_new : m_run;
+        const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
+        const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
+
+        // P_t's buffer (and O_t) are free once the previous PV of this unit finished (the
+        // previous unit's last PV was waited for by its epilogue).  That PV ran while this
+        // iteration loaded S and exchanged the row max, so the wait is normally short, and
+        // p can then go to shared memory as it is computed.
+        if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (gi - 1) & 1u, SITE_SOFTMAX));
+        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 2);
+        float2 sum = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
+        if (ok) {
+          const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-moff, -moff);
+          // Chunks with no masked entry evaluate a quarter of the exponentials on the FMA
+          // pipe; masked chunks use ex2 only, so masked entries stay exactly zero.
+          if (rel >= 63) {
+            exp_chunk_store<true>(s0, ptile, r, 8 * h, sc2, nm2, sum);
+            exp_chunk_store<true>(s1, ptile, r, 8 * h + 4, sc2, nm2, sumb);
+          } else {
+            exp_chunk_store<false>(s0, ptile, r, 8 * h, sc2, nm2, sum);
+            exp_chunk_store<false>(s1, ptile, r, 8 * h + 4, sc2, nm2, sumb);
+          }
+          fence_proxy_async_smem();
+          if (j > 0 && __any_sync(0xffffffffu, need)) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + 32 * c, o);
+              tmem_wait_ld_dep(o);
+#pragma unroll
+              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+              tmem_st32(tO + 32 * c, o);
+            }
+            tmem_wait_st();
+          }
+          tc_fence_before();
+          mbar_arrive(bar(pready_bar(t)));
+        }
+        l_run = l_run * alpha + ((sum.x + sum.y) + (sumb.x + sumb.y));
+        m_run = m_use;
+        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 3);
+      }
+
+      // The next unit's Q was loaded once this unit's last QK^T finished: rotate and
+      // release it now, so its first QK^T overlaps this unit's epilogue.
+      if (inext < n_rounds) prepare_q(decode(unit_of(inext)), (uc + 1) & 1, uc + 1);
+      // ---- epilogue: O / l -> bf16 -> P_t's buffer (free once the last PV is done) ->
+      // one TMA store per 64-dim half of the tile
+      const uint32_t last = Gb + n_kv - 1;
+      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, uc, 4);
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), last & 1u, SITE_EPILOGUE));
+      named_bar_sync(bar_free, 256);
+      xchg[h * 128 + r] = l_run;
+      named_bar_sync(bar_x, 256);
+      const float l_tot = l_run + xchg[(1 - h) * 128 + r];
       if (ok) {
         tc_fence_after();
-        tmem_ld32(tS + 0, s0);
-        tmem_ld32(tS + 32, s1);
-        tmem_wait_ld_dep(s0);
-        reg_dep(s1);
-        tc_fence_before();
-        mbar_arrive(bar(B_SFREE));  // S_t may now be overwritten by the next QK^T
-      } else {
-#pragma unroll
-        for (int k = 0; k < 32; ++k) s0[k] = s1[k] = 0xFF800000u;
-      }
-
-      const int rel = lim - j * kBN - 64 * h;  // columns (of this half) > rel are masked
-      if (rel < 63) {
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          if (k > rel) s0[k] = 0xFF800000u;
-          if (k + 32 > rel) s1[k] = 0xFF800000u;
-        }
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        mx0 = fmax3(mx0, __uint_as_float(s0[k]), __uint_as_float(s0[k + 1]));
-        mx1 = fmax3(mx1, __uint_as_float(s1[k]), __uint_as_float(s1[k + 1]));
-      }
-      // row max over both halves: slot [h][r] <-> [1-h][r]
-      named_bar_sync(bar_free, 256);  // everyone has read the previous iteration's slots
-      xchg[h * 128 + r] = fmaxf(mx0, mx1);
-      named_bar_sync(bar_x, 256);
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), xchg[(1 - h) * 128 + r]) * sl2;
-      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 1);
-      const float m_new = fmaxf(m_run, m_tile);
-      const bool need = m_new > m_run + kRescaleLog2;
-      const float m_use = need ? m_new : m_run;
-      const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
-      const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
-
-      uint32_t pw[32];
-      float2 sum = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
-      const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-moff, -moff);
-      // Chunks with no masked entry evaluate a quarter of the exponentials on the FMA
-      // pipe; masked chunks use ex2 only, so masked entries stay exactly zero.
-      if (rel >= 63) {
-        exp_chunk<true>(s0, pw, 0, sc2, nm2, sum);
-        exp_chunk<true>(s1, pw, 16, sc2, nm2, sumb);
-      } else {
-        exp_chunk<false>(s0, pw, 0, sc2, nm2, sum);
-        exp_chunk<false>(s1, pw, 16, sc2, nm2, sumb);
-      }
-
-      // P_t's buffer (and O_t) are free once the previous PV finished.
-      if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (j - 1) & 1, SITE_SOFTMAX));
-      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 2);
-      if (ok) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(ptile + sw128_chunk(r, 8 * h + c)) =
-              make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
-        fence_proxy_async_smem();
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-          tc_fence_after();
+        const float inv_l = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld_dep(o);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld_dep(o);
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-            tmem_st32(tO + 32 * c, o);
+          for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte chunk
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(ptile + sw128_chunk(r, 8 * h + c * 4 + q)) = v;
           }
-          tmem_wait_st();
         }
-        tc_fence_before();
-        mbar_arrive(bar(B_PREADY));
+        tc_fence_before();  // O_t may be overwritten by the next unit's first PV
       }
-      l_run = l_run * alpha + ((sum.x + sum.y) + (sumb.x + sumb.y));
-      m_run = m_use;
-      if (r == 0 && h == 0) PF_TRACE(2 + t, j, 3);
-    }
-
-    // ---- epilogue: O / l -> bf16 -> (reuse the Q tile smem) -> TMA store
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (n_kv - 1) & 1, SITE_EPILOGUE));
-    named_bar_sync(bar_free, 256);
-    xchg[h * 128 + r] = l_run;
-    named_bar_sync(bar_x, 256);
-    const float l_tot = l_run + xchg[(1 - h) * 128 + r];
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + 32 * c, o);
-        tmem_wait_ld_dep(o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte chunk
-          uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
-          v.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
-          v.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
-          v.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(qtile + sw128_chunk(r, 8 * h + c * 4 + q)) = v;
-        }
+      fence_proxy_async_smem();
+      named_bar_sync(bar_x, 256);
+      const int p0 = x.p0 + t * kRowsPerHead;
+      if (ok && h == 0 && r == 0 && p0 < p.S) {  // a tile starting past the sequence has nothing to store
+        const uint32_t src = sbase + kOffP + t * kTileBytes;
+        tma_store_3d(&tmO, src, 0, p0, x.zq);
+        tma_store_3d(&tmO, src + kHalf, 64, p0, x.zq);
+        bulk_commit();
+        store_pending = true;
       }
+      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, uc, 5);
+      Gb += n_kv;
+      ++uc;
     }
-    fence_proxy_async_smem();
-    named_bar_sync(bar_x, 256);
-    if (ok && h == 0 && r == 0 && p0 < p.S) {  // a tile starting past the sequence has nothing to store
-      const uint32_t src = sbase + kOffQ + t * kTileBytes;
-      tma_store_3d(&tmO, src, 0, p0, zq);
-      tma_store_3d(&tmO, src + kHalf, 64, p0, zq);
-      bulk_commit();
-      bulk_wait0();
-    }
+    if (h == 0 && r == 0) bulk_wait0();
   }
 
   // ---- teardown: everyone done with TMEM and shared memory
@@ -610,8 +820,8 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return GQA_ERR_MISALIGNED;
   if ((flags & (GQA_FLAG_ROPE_Q | GQA_FLAG_ROPE_K)) && (!aligned16(cos) || !aligned16(sin))) return GQA_ERR_MISALIGNED;
   const long long n_qblocks = (S + kPosPerCta - 1) / kPosPerCta;
-  const long long grid = n_qblocks * B * kv_count;
-  if (grid > 0x7FFFFFFFLL || static_cast<long long>(B) * Hq > 0x7FFFFFFFLL) return GQA_ERR_UNSUPPORTED;
+  const long long n_units = n_qblocks * B * kv_count;
+  if (n_units > 0x7FFFFFFFLL || static_cast<long long>(B) * Hq > 0x7FFFFFFFLL) return GQA_ERR_UNSUPPORTED;
 
   CUtensorMap tmQ, tmK, tmV, tmO;
   int rc;
@@ -625,6 +835,19 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   static std::atomic<uint64_t> attr_done{0}, attr_done_tr{0};
   if ((rc = ensure_smem_attr(prefill_kernel<false>, kSmemBytes, attr_done)) != GQA_OK) return rc;
   if (trace && (rc = ensure_smem_attr(prefill_kernel<true>, kSmemBytes, attr_done_tr)) != GQA_OK) return rc;
+  // The register split assumes the kernel was compiled to kRegsLaunch registers per thread.
+  static std::atomic<int> regs_ok{0};
+  if (regs_ok.load(std::memory_order_acquire) == 0) {
+    cudaFuncAttributes fa, fb;
+    if (cudaFuncGetAttributes(&fa, prefill_kernel<false>) != cudaSuccess ||
+        cudaFuncGetAttributes(&fb, prefill_kernel<true>) != cudaSuccess)
+      return GQA_ERR_CUDA;
+    regs_ok.store(fa.numRegs == kRegsLaunch && fb.numRegs == kRegsLaunch ? 1 : -1, std::memory_order_release);
+  }
+  if (regs_ok.load(std::memory_order_acquire) < 0) return GQA_ERR_UNSUPPORTED;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   Params p;
   p.B = B;
   p.S = S;
@@ -633,17 +856,23 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   p.kv_begin = kv_begin;
   p.kv_count = kv_count;
   p.n_qblocks = static_cast<int>(n_qblocks);
+  p.n_units = static_cast<int>(n_units);
   p.flags = flags;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.cos = static_cast<const uint16_t*>(cos);
   p.sin = static_cast<const uint16_t*>(sin);
   p.trace = trace;
   p.trace_block = trace_block;
+  const int grid = static_cast<int>(n_units < sms ? n_units : sms);
   if (trace)
-    prefill_kernel<true><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
+    prefill_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
   else
-    prefill_kernel<false><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
+    prefill_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 
+}  // namespace gqa
+
+namespace gqa {
+GQA_ERROR_FLAG_ACCESSOR(error_flag_prefill)
 }  // namespace gqa

@@ -18,7 +18,7 @@
 
 namespace gqa {
 
-__device__ int g_gqa_dev_error = 0;
+GQA_ERROR_FLAG_ACCESSOR(error_flag_stages)
 
 namespace {
 
