@@ -68,6 +68,69 @@ class PrefillSession:
         return out_h
 
 
+class PrefillStream:
+    """Host-buffer prefill over a sequence of steps with the copies overlapped.
+
+    Two device buffer sets and three CUDA streams: while step i computes, step i+1's
+    Q/K/V go host->device and step i-1's O goes device->host, so a step costs the
+    slowest of the three instead of their sum.  Every step still copies its own inputs
+    in and its output out.  ``run`` enqueues everything and makes the caller's current
+    stream wait for the last copy-out; synchronise (or record an event) after it.
+    """
+
+    def __init__(self, B: int, S: int, Hq: int, Hkv: int, head_dim: int = 128, *, causal: bool = True,
+                 rope: str = "prepass_k", theta: float = kernels.ROPE_THETA, device=None):
+        self.device = torch.device(device or "cuda")
+        self.sets = [PrefillSession(B, S, Hq, Hkv, head_dim, causal=causal, rope=rope, theta=theta, device=self.device)
+                     for _ in range(2)]
+        self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream(self.device) for _ in range(3))
+
+    def h2d_bytes(self) -> int:
+        return self.sets[0].h2d_bytes()
+
+    def d2h_bytes(self) -> int:
+        return self.sets[0].d2h_bytes()
+
+    def launches_per_step(self) -> int:
+        return self.sets[0].launches_per_step()
+
+    def run(self, steps) -> None:
+        """steps: iterable of (q_h, k_h, v_h, out_h) bf16 CPU tensors (pinned)."""
+        cur = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(cur)
+        for st in (self.s_in, self.s_comp, self.s_out):
+            st.wait_event(start)
+        ev_comp, ev_out = [], []
+        last = None
+        for i, (q_h, k_h, v_h, out_h) in enumerate(steps):
+            sess = self.sets[i % 2]
+            with torch.cuda.stream(self.s_in):
+                if i >= 2:  # this buffer set's inputs were consumed by step i-2
+                    self.s_in.wait_event(ev_comp[i - 2])
+                sess.q.copy_(q_h, non_blocking=True)
+                sess.k.copy_(k_h, non_blocking=True)
+                sess.v.copy_(v_h, non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(self.s_in)
+            with torch.cuda.stream(self.s_comp):
+                self.s_comp.wait_event(ev_in)
+                if i >= 2:  # and its output was read out by step i-2's copy
+                    self.s_comp.wait_event(ev_out[i - 2])
+                sess.run_device()
+                e = torch.cuda.Event()
+                e.record(self.s_comp)
+                ev_comp.append(e)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(e)
+                out_h.copy_(sess.o, non_blocking=True)
+                last = torch.cuda.Event()
+                last.record(self.s_out)
+                ev_out.append(last)
+        if last is not None:
+            cur.wait_event(last)
+
+
 class DecodeSession:
     def __init__(self, B: int, Lmax: int, Hq: int, Hkv: int, head_dim: int = 128, *, split_len: int = 0,
                  rope_q: bool = True, theta: float = kernels.ROPE_THETA, device=None):

@@ -204,3 +204,24 @@ def test_kv_head_shard_writes_only_its_heads():
     assert torch.isnan(out[:, :8].float()).all() and torch.isnan(out[:, 20:].float()).all()
     full = kernels.prefill(q, k, v)
     assert torch.equal(full[:, 8:20], out[:, 8:20])
+
+
+def test_prefill_stream_overlapped_host_steps_match_device_results():
+    """PrefillStream: each step's host output equals the device-resident result of its inputs."""
+    from llama3_8b_attention_optimize_b200.session import PrefillStream
+    B, Hq, Hkv, S = 1, 32, 8, 256
+    pipe = PrefillStream(B, S, Hq, Hkv)
+    steps, refs = [], []
+    cos, sin = kernels.rope_cache(S)
+    for i in range(5):
+        q = randn_bf16((B, Hq, S, 128), 300 + i)
+        k = randn_bf16((B, Hkv, S, 128), 400 + i)
+        v = randn_bf16((B, Hkv, S, 128), 500 + i)
+        refs.append(kernels.prefill(q, kernels.rope(k, cos, sin), v, cos, sin, rope_q=True).cpu())
+        steps.append((q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory(),
+                      torch.empty(B, Hq, S, 128, dtype=torch.bfloat16).pin_memory()))
+    pipe.run(steps)
+    torch.cuda.synchronize()
+    kernels.device_check()
+    for (_, _, _, out), ref in zip(steps, refs):
+        assert torch.equal(out, ref)
