@@ -39,6 +39,8 @@ int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {
 // Per-file device error words (see GQA_ERROR_FLAG_ACCESSOR): value, optionally cleared.
 int error_flag_stages(bool clear);
 int error_flag_prefill(bool clear);
+int error_flag_prefill7(bool clear);
+int error_flag_prefill8(bool clear);
 int error_flag_decode(bool clear);
 int error_flag_decode_tc(bool clear);
 int error_flag_gemm(bool clear);
@@ -46,6 +48,14 @@ int error_flag_gemm(bool clear);
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
                    cudaStream_t stream, long long* trace = nullptr, int trace_block = -1);
+
+int launch_prefill7(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B,
+                    int S, int Hq, int Hkv, int kv_begin, int kv_count, float scale, int flags, cudaStream_t stream,
+                    long long* trace = nullptr, int trace_block = -1);
+
+int launch_prefill8(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B,
+                    int S, int Hq, int Hkv, int kv_begin, int kv_count, float scale, int flags, cudaStream_t stream,
+                    long long* trace = nullptr, int trace_block = -1);
 
 int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
                      const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,
