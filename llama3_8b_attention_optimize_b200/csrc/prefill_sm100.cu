@@ -108,7 +108,15 @@ enum : int {
 //   2: QK0(j+1) PV0(j) QK1(j+1) PV1(j), hand-offs per tile (the tiles' softmax phases
 //      half an iteration apart)
 constexpr int kMmaOrder = 1;
+// One mbarrier arrival per softmax warp (after __syncwarp) instead of one per thread
+// (measured no faster here; the per-thread arrivals are kept).
+constexpr bool kWarpArrive = false;
+constexpr int kArriveDiv = kWarpArrive ? 32 : 1;
 constexpr int kHandoffThreads = kMmaOrder == 0 ? kSoftmaxThreads : kSoftmaxThreads / 2;
+// Exponentials of unmasked chunks partly on the FMA pipe (a cubic fit of 2^f, a quarter
+// of the pairs): with the bf16-consistent row sums below the kernel is MUFU-bound enough
+// for this to pay (about 10 % measured).
+constexpr bool kEmulateExp = true;
 __device__ __forceinline__ int sfree_bar(int t) { return B_SFREE + (kMmaOrder == 0 ? 0 : t); }
 __device__ __forceinline__ int pready_bar(int t) { return B_PREADY + (kMmaOrder == 0 ? 0 : t); }
 constexpr int kKReadySlots = 4;
@@ -165,7 +173,10 @@ __device__ __forceinline__ void exp_chunk_store(const uint32_t (&s)[32], uint8_t
         y.y = ex2_approx(x.y);
       }
       w[e] = pack_bf16x2(y.x, y.y);
-      // the row sum uses the bf16 values PV multiplies, so O / l normalises exactly them
+      // The row sum adds the bf16 values PV multiplies, so O / l is a weighted mean with
+      // weights summing to exactly 1.  (Summing the unrounded fp32 p saves ~1 instruction
+      // per score but lets the weights' rounding bias O by up to 2^-8 relative, which
+      // exceeds the 1e-2 absolute tolerance for |O| near 2.)
       add_bf16x2_to_f32(acc, w[e]);
     }
     *reinterpret_cast<uint4*>(ptile + sw128_chunk(r, c0 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -191,6 +202,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
+  // softmax hand-off: the whole warp (converged) arrives once, or each thread does
+  auto warp_arrive = [&](uint32_t b) {
+    if (kWarpArrive) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b);
+    } else {
+      mbar_arrive(b);
+    }
+  };
 
   const bool causal = (p.flags & GQA_FLAG_CAUSAL) != 0;
   const bool rope_q = (p.flags & GQA_FLAG_ROPE_Q) != 0;
@@ -221,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B_QFULL + t), 1);
-      mbar_init(bar(B_QREADY + t), 256);
+      mbar_init(bar(B_QREADY + t), 256 / kArriveDiv);
       mbar_init(bar(B_SFULL + t), 1);
       mbar_init(bar(B_PVDONE + t), 1);
     }
@@ -232,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int k = 0; k < kKReadySlots; ++k) mbar_init(bar(B_KREADY + k), 64);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(B_SFREE + t), kHandoffThreads);
-      mbar_init(bar(B_PREADY + t), kHandoffThreads);
+      mbar_init(bar(B_SFREE + t), kHandoffThreads / kArriveDiv);
+      mbar_init(bar(B_PREADY + t), kHandoffThreads / kArriveDiv);
     }
     mbar_init(bar(B_DRAIN), 1);
     fence_mbar_init();
@@ -537,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         rope_row_smem_part(smem + kOffQ + t * kTileBytes, kHalf, r, p.cos + static_cast<size_t>(pos) * kD,
                            p.sin + static_cast<size_t>(pos) * kD, 4 * h);
       fence_proxy_async_smem();
-      mbar_arrive(bar(B_QREADY + t));
+      warp_arrive(bar(B_QREADY + t));
       if (r == 0 && h == 0 && t == 0) PF_TRACE(5, unit_no, 3);
     };
     {
@@ -581,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld_dep(s0);
           reg_dep(s1);
           tc_fence_before();
-          mbar_arrive(bar(sfree_bar(t)));  // S_t may now be overwritten by the next QK^T
+          warp_arrive(bar(sfree_bar(t)));  // S_t may now be overwritten by the next QK^T
         } else {
 #pragma unroll
           for (int k = 0; k < 32; ++k) s0[k] = s1[k] = 0xFF800000u;
@@ -628,11 +648,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float2 sum = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
         if (ok) {
           const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-moff, -moff);
-          // Chunks with no masked entry evaluate a quarter of the exponentials on the FMA
-          // pipe; masked chunks use ex2 only, so masked entries stay exactly zero.
+          // Chunks with no masked entry may evaluate part of the exponentials on the FMA
+          // pipe (kEmulateExp); masked chunks use ex2 only, so masked entries stay zero.
           if (rel >= 63) {
-            exp_chunk_store<true>(s0, ptile, r, 8 * h, sc2, nm2, sum);
-            exp_chunk_store<true>(s1, ptile, r, 8 * h + 4, sc2, nm2, sumb);
+            exp_chunk_store<kEmulateExp>(s0, ptile, r, 8 * h, sc2, nm2, sum);
+            exp_chunk_store<kEmulateExp>(s1, ptile, r, 8 * h + 4, sc2, nm2, sumb);
           } else {
             exp_chunk_store<false>(s0, ptile, r, 8 * h, sc2, nm2, sum);
             exp_chunk_store<false>(s1, ptile, r, 8 * h + 4, sc2, nm2, sumb);
@@ -652,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
           }
           tc_fence_before();
-          mbar_arrive(bar(pready_bar(t)));
+          warp_arrive(bar(pready_bar(t)));
         }
         l_run = l_run * alpha + ((sum.x + sum.y) + (sumb.x + sumb.y));
         m_run = m_use;
