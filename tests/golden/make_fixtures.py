@@ -16,6 +16,10 @@ Writes:
   The SHA-256 of every hex file is checked against
   golden_fpga_slice_data/attention_fpga_slice_manifest.json where listed.
 
+* ``fpga_slice_sha256.json`` -- the SHA-256 that the reference's manifest lists for
+  each of those hex files (upper-case hex convention), so emitted hex files can be
+  checked byte for byte.
+
 * ``layer_s32.npz`` -- every stage dump of the reference's own
   ``run_full_attention`` (llama3_attention_golden_model.py:144-197), imported
   and run here on seeded synthetic inputs: hidden [32, 4096] ~ N(0,1) and
@@ -114,6 +118,20 @@ def make_fpga_slice(ref: str) -> dict:
     return out
 
 
+def slice_sha256(ref: str) -> dict:
+    """Manifest SHA-256 of each slice hex file, plus a digest of the full 8192-token RoPE
+    ROM words (``rom_<sin|cos>_words``: SHA-256 of the little-endian uint16 words of
+    RoPE/<sin|cos>_bf16_all.hex, which has CRLF line ends)."""
+    gd = os.path.join(ref, "A_attention_integration_final_v5/tb/golden_fpga_slice_data")
+    with open(os.path.join(gd, "attention_fpga_slice_manifest.json")) as f:
+        manifest = json.load(f)["outputs"]
+    out = {name: entry["sha256"] for name, entry in sorted(manifest.items()) if "sha256" in entry}
+    for name in ("sin", "cos"):
+        words = _hex(os.path.join(ref, "RoPE", f"{name}_bf16_all.hex"))
+        out[f"rom_{name}_words"] = hashlib.sha256(words.astype("<u2").tobytes()).hexdigest()
+    return out
+
+
 def _import_golden(ref: str):
     spec = importlib.util.spec_from_file_location(
         "llama3_attention_golden_model", os.path.join(ref, "llama3_attention_golden_model.py"))
@@ -151,6 +169,9 @@ def main() -> None:
     args = ap.parse_args()
     fs = make_fpga_slice(args.reference)
     np.savez_compressed(os.path.join(HERE, "fpga_slice.npz"), **fs)
+    with open(os.path.join(HERE, "fpga_slice_sha256.json"), "w") as f:
+        json.dump(slice_sha256(args.reference), f, indent=1)
+        f.write("\n")
     layer = make_layer(args.reference)
     np.savez_compressed(os.path.join(HERE, "layer_s32.npz"), **layer)
     for name in ("fpga_slice.npz", "layer_s32.npz"):
