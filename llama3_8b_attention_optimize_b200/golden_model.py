@@ -16,6 +16,9 @@ function                 reference                                    computed b
 ``run_full_attention``   :144-197 (all stage dumps)                   tcgen05 GEMMs + stage kernels
 ``run_attention_core``   :157-190 without the projections             stage kernels / fused kernel
 ``save_dump``            :214-246 (full/ and fpga_slice/ .npy files)  host write
+``get_layer0_weight_paths`` :59-93 (index.json shard map / single file)  host (no network)
+``load_layer0_weights``  :96-121                                      safetensors read
+``main``                 :201-249 (load, seeded input, run, dump)     all of the above
 =======================  ===========================================  ==========================
 
 With ``debug=True`` (the default, the reference's behaviour) every stage is
@@ -25,6 +28,7 @@ S x S stages are omitted from the dump.
 """
 from __future__ import annotations
 
+import json
 import os
 
 import numpy as np
@@ -32,6 +36,9 @@ import torch
 
 from . import kernels
 
+MODEL_REPO = "NousResearch/Meta-Llama-3-8B"
+LOCAL_SAFETENSORS_DIR = "../llama3_weights"
+OUTPUT_DIR = "./golden_model_outputs"
 LAYER_IDX = 0
 SEQ_LEN = 256
 HIDDEN_SIZE = 4096
@@ -94,6 +101,58 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     dev = x.device if x.is_cuda else _dev()
     y = kernels.rope(_to_gpu_bf16(x, dev), _to_gpu_bf16(cos, dev), _to_gpu_bf16(sin, dev))
     return _back(y, x)
+
+
+def _layer_weight_names(layer: int) -> list:
+    return [f"model.layers.{layer}.self_attn.{n}_proj.weight" for n in ("q", "k", "v", "o")]
+
+
+def get_layer0_weight_paths(local_dir: str | None = LOCAL_SAFETENSORS_DIR, layer: int = LAYER_IDX) -> dict:
+    """Tensor name -> safetensors file for the layer's q/k/v/o_proj weights (reference
+    :59-93).  A local directory with ``model.safetensors.index.json`` is resolved through
+    its weight map, otherwise ``model.safetensors`` in it holds everything; with no local
+    directory the files come from the Hugging Face cache / hub (``MODEL_REPO``), which
+    needs network access or a populated cache."""
+    names = _layer_weight_names(layer)
+    if local_dir is not None and os.path.isdir(local_dir):
+        index_path = os.path.join(local_dir, "model.safetensors.index.json")
+        if os.path.exists(index_path):
+            with open(index_path, "r") as f:
+                weight_map = json.load(f)["weight_map"]
+            missing = [n for n in names if n not in weight_map]
+            if missing:
+                raise KeyError(f"{index_path}: no entry for {missing}")
+            return {n: os.path.join(local_dir, weight_map[n]) for n in names}
+        return {n: os.path.join(local_dir, "model.safetensors") for n in names}
+    from huggingface_hub import hf_hub_download
+
+    with open(hf_hub_download(repo_id=MODEL_REPO, filename="model.safetensors.index.json"), "r") as f:
+        weight_map = json.load(f)["weight_map"]
+    shards: dict = {}
+    out = {}
+    for n in names:
+        shard = weight_map[n]
+        if shard not in shards:
+            shards[shard] = hf_hub_download(repo_id=MODEL_REPO, filename=shard)
+        out[n] = shards[shard]
+    return out
+
+
+def load_layer0_weights(local_dir: str | None = LOCAL_SAFETENSORS_DIR, layer: int = LAYER_IDX):
+    """(q_proj, k_proj, v_proj, o_proj) as fp32 CPU tensors holding bf16 values, HF
+    [out, in] layout (reference :96-121)."""
+    from safetensors import safe_open
+
+    paths = get_layer0_weight_paths(local_dir, layer)
+    opened = {}
+    weights = {}
+    for name, path in paths.items():
+        if path not in opened:
+            opened[path] = safe_open(path, framework="pt")
+        if name not in opened[path].keys():
+            raise KeyError(f"{path}: tensor {name} not found")
+        weights[name] = opened[path].get_tensor(name)
+    return tuple(to_bf16(weights[n].float()) for n in _layer_weight_names(layer))
 
 
 def run_attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
@@ -166,3 +225,22 @@ def save_dump(dump: dict, output_dir: str = "./golden_model_outputs", weights: d
     os.makedirs(fdir, exist_ok=True)
     for key, t in fpga_slice(dump).items():
         np.save(os.path.join(fdir, f"{key}.npy"), t.detach().cpu().numpy())
+
+
+def main(local_dir: str | None = LOCAL_SAFETENSORS_DIR, output_dir: str = OUTPUT_DIR, seq_len: int = SEQ_LEN,
+         device=None) -> dict:
+    """The reference's main() (:201-249) on the B200: load layer-0 weights, draw the
+    seeded bf16 input (torch.manual_seed(42), N(0, 0.02^2) [seq_len, 4096]), run every
+    stage and write full/ and fpga_slice/ dumps (weights and input included).  Returns
+    the dump."""
+    q_proj, k_proj, v_proj, o_proj = load_layer0_weights(local_dir)
+    torch.manual_seed(42)
+    hidden_states = to_bf16(torch.randn(seq_len, HIDDEN_SIZE) * 0.02)
+    if device is not None:
+        dev = torch.device(device)
+        hidden_states, q_proj, k_proj, v_proj, o_proj = (t.to(dev) for t in
+                                                         (hidden_states, q_proj, k_proj, v_proj, o_proj))
+    dump = run_full_attention(hidden_states, q_proj, k_proj, v_proj, o_proj)
+    save_dump(dump, output_dir, weights={"hidden_states_input": hidden_states, "q_proj": q_proj,
+                                         "k_proj": k_proj, "v_proj": v_proj, "o_proj": o_proj})
+    return dump
