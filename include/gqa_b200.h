@@ -43,6 +43,7 @@ typedef struct CUstream_st* gqa_stream_t; /* == cudaStream_t */
 #define GQA_ERR_DEVICE_TIMEOUT (-5)   /* a kernel's bounded wait expired */
 #define GQA_ERR_WORKSPACE (-6)        /* workspace missing or too small */
 #define GQA_ERR_NO_DEVICE (-7)        /* no usable sm_100 device */
+#define GQA_ERR_DEVICE_INPUT (-8)     /* a kernel found invalid device-side input data */
 
 #define GQA_FLAG_CAUSAL 1 /* mask keys j > i (golden :180-181) */
 #define GQA_FLAG_ROPE_Q 2 /* rotate Q in the kernel (golden apply_rope :162-163) */
@@ -57,7 +58,9 @@ const char* gqa_strerror(int code);
 int gqa_version(void);
 
 /* Synchronize `stream`, then report (and clear) the sticky device error:
- * GQA_OK, GQA_ERR_DEVICE_TIMEOUT (site code in *site if non-NULL) or GQA_ERR_CUDA. */
+ * GQA_OK, GQA_ERR_DEVICE_TIMEOUT (a bounded wait gave up), GQA_ERR_DEVICE_INPUT (a
+ * device-side check of input data failed: block-table entry or cache capacity), with
+ * the site code in *site if non-NULL, or GQA_ERR_CUDA. */
 int gqa_device_check(gqa_stream_t stream, int* site);
 
 /* ---------------------------------------------------------------- RoPE
@@ -145,6 +148,38 @@ int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const void* vcach
                             const int32_t* q_pos, const void* cos, const void* sin, void* o, int B, int max_len,
                             int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
                             float scale, int flags, gqa_stream_t stream);
+
+/* ---------------------------------------------------------------- paged K/V cache
+ * The step after decode (the reference has no serving cache): append each step's new
+ * K/V rows to the cache, rotating K at its position, and decode over a paged cache.
+ *
+ * Paged layout: K and V page pools [num_pages][Hkv][page_size][head_dim] bf16; token j
+ * of sequence b is row j % page_size of page block_table[b * max_pages_per_seq +
+ * j / page_size] (int32, device).  page_size must be a multiple of 128 for decode.
+ *
+ * gqa_kv_append_bf16: k_new/v_new [B][Hkv][n_new][128]; token i of sequence b goes to
+ * position lens[b] + i.  block_table == NULL selects the contiguous cache
+ * [B][Hkv][max_len][128] (max_len used only then).  GQA_FLAG_ROPE_K rotates K with
+ * cos/sin rows [pos] (tables of >= capacity rows, as gqa_rope_cache_bf16 builds them),
+ * bit-identical to gqa_rope_bf16 / the golden apply_rope.  If lens_out is non-NULL a
+ * second launch writes lens_out[b] = lens[b] + n_new (lens_out may equal lens).
+ * Positions past the cache or block-table entries outside [0, num_pages) skip their
+ * row and set GQA_ERR_DEVICE_INPUT for gqa_device_check.
+ *
+ * gqa_decode_paged_bf16: gqa_decode_bf16 over the paged cache (capacity
+ * max_pages_per_seq * page_size keys per sequence, lens[b] <= capacity); split_len a
+ * multiple of 128 (0 = default); workspace = gqa_decode_workspace_size(B, Hq,
+ * capacity, split_len).  Results are bit-identical to gqa_decode_bf16 on a contiguous
+ * cache holding the same rows.                                                    */
+int gqa_kv_append_bf16(const void* k_new, const void* v_new, void* kcache, void* vcache, const int32_t* block_table,
+                       int max_pages_per_seq, int page_size, int num_pages, const int32_t* lens, int32_t* lens_out,
+                       const void* cos, const void* sin, int B, int Hkv, int n_new, int head_dim, int max_len,
+                       int flags, gqa_stream_t stream);
+int gqa_decode_paged_bf16(const void* q, const void* kpages, const void* vpages, const int32_t* block_table,
+                          int max_pages_per_seq, int page_size, int num_pages, const int32_t* lens,
+                          const int32_t* q_pos, const void* cos, const void* sin, void* o, void* workspace,
+                          size_t workspace_bytes, int B, int Hq, int Hkv, int head_dim, int kv_head_begin,
+                          int kv_head_count, int split_len, float scale, int flags, gqa_stream_t stream);
 
 /* ---------------------------------------------------------------- projections
  * The full layer's linear maps (golden run_full_attention,

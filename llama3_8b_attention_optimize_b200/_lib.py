@@ -20,6 +20,7 @@ GQA_ERR_CUDA = -4
 GQA_ERR_DEVICE_TIMEOUT = -5
 GQA_ERR_WORKSPACE = -6
 GQA_ERR_NO_DEVICE = -7
+GQA_ERR_DEVICE_INPUT = -8
 
 GQA_FLAG_CAUSAL = 1
 GQA_FLAG_ROPE_Q = 2
@@ -47,6 +48,10 @@ SIGNATURES = {
     "gqa_decode_noalloc_scratch_bytes": (_sz, []),
     "gqa_decode_bf16_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _i,
                                      _vp]),
+    "gqa_kv_append_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                                _vp]),
+    "gqa_decode_paged_bf16": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i,
+                                   _i, _i, _i, _f, _i, _vp]),
     "gqa_gemm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_qkv_proj_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_o_proj_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),

@@ -79,6 +79,7 @@ extern "C" const char* gqa_strerror(int code) {
     case GQA_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired (device error flag set)";
     case GQA_ERR_WORKSPACE: return "workspace missing or too small";
     case GQA_ERR_NO_DEVICE: return "no usable sm_100 device / driver entry point";
+    case GQA_ERR_DEVICE_INPUT: return "a kernel found invalid device-side input (page index or cache capacity)";
     default: return "unknown status";
   }
 }
@@ -89,7 +90,7 @@ extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   if (site) *site = 0;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return GQA_ERR_CUDA;
   int (*const readers[])(bool) = {error_flag_stages,   error_flag_prefill,   error_flag_prefill7, error_flag_prefill8,
-                                   error_flag_decode, error_flag_decode_tc, error_flag_gemm};
+                                   error_flag_decode, error_flag_decode_tc, error_flag_gemm,     error_flag_kvcache};
   int first = 0;
   for (auto rd : readers) {  // read and clear every file's word; report the first set one
     const int v = rd(true);
@@ -98,7 +99,8 @@ extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   }
   if (first == 0) return GQA_OK;
   if (site) *site = first;
-  return GQA_ERR_DEVICE_TIMEOUT;
+  // sites 0x300-0x3ff are checks of device-side input data, the rest are bounded waits
+  return (first >= 0x300 && first < 0x400) ? GQA_ERR_DEVICE_INPUT : GQA_ERR_DEVICE_TIMEOUT;
 }
 
 extern "C" int gqa_prefill_bf16(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin,

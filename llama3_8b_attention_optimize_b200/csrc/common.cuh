@@ -22,17 +22,24 @@ namespace gqa {
 // force), so each keeps its own word; GQA_ERROR_FLAG_ACCESSOR gives the host a
 // reader per file, and gqa_device_check() polls them all.
 static __device__ int g_gqa_dev_error = 0;
+// Second word for checks of device-side input data (a block-table entry, a cache
+// position): the kernel carries on with a safe substitute, so unlike a failed wait it
+// does not make the other threads' waits give up.
+static __device__ int g_gqa_dev_input_error = 0;
 
-// Host reader of this file's error word (optionally clearing it); -1 on a CUDA error.
-#define GQA_ERROR_FLAG_ACCESSOR(fn)                                                      \
-  int fn(bool clear) {                                                                   \
-    int v = 0;                                                                           \
-    if (cudaMemcpyFromSymbol(&v, g_gqa_dev_error, sizeof(int)) != cudaSuccess) return -1; \
-    if (clear && v != 0) {                                                               \
-      const int z = 0;                                                                   \
-      if (cudaMemcpyToSymbol(g_gqa_dev_error, &z, sizeof(int)) != cudaSuccess) return -1; \
-    }                                                                                    \
-    return v;                                                                            \
+// Host reader of this file's error words (optionally clearing them): the failed-wait
+// site if any, else the input-check site, else 0; -1 on a CUDA error.
+#define GQA_ERROR_FLAG_ACCESSOR(fn)                                                              \
+  int fn(bool clear) {                                                                           \
+    int v = 0, w = 0;                                                                            \
+    if (cudaMemcpyFromSymbol(&v, g_gqa_dev_error, sizeof(int)) != cudaSuccess) return -1;         \
+    if (cudaMemcpyFromSymbol(&w, g_gqa_dev_input_error, sizeof(int)) != cudaSuccess) return -1;   \
+    if (clear && (v != 0 || w != 0)) {                                                           \
+      const int z = 0;                                                                           \
+      if (cudaMemcpyToSymbol(g_gqa_dev_error, &z, sizeof(int)) != cudaSuccess) return -1;         \
+      if (cudaMemcpyToSymbol(g_gqa_dev_input_error, &z, sizeof(int)) != cudaSuccess) return -1;   \
+    }                                                                                            \
+    return v != 0 ? v : w;                                                                       \
   }
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -49,6 +56,10 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 
 __device__ __forceinline__ void record_error(int site) {
   atomicCAS(&g_gqa_dev_error, 0, site);
+}
+
+__device__ __forceinline__ void record_input_error(int site) {
+  atomicCAS(&g_gqa_dev_input_error, 0, site);
 }
 
 __device__ __forceinline__ bool error_pending() {
@@ -98,6 +109,19 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int sit
         record_error(site);
         return false;
       }
+    }
+  }
+}
+
+// Wait for this CTA's own asynchronous work (TMA loads, tensor-core ops) before it exits
+// or frees TMEM: bounded by time only, not cut short by another thread's error.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int site) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      record_error(site);
+      return false;
     }
   }
 }

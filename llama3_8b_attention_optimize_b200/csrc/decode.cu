@@ -309,6 +309,41 @@ extern "C" int gqa_decode_bf16(const void* q, const void* kcache, const void* vc
 }
 
 // ---------------------------------------------------------------------------
+// Decode over a paged K/V cache: the same tensor-core split-KV kernel, its TMA
+// producer resolving each 128-key chunk through the block table.
+extern "C" int gqa_decode_paged_bf16(const void* q, const void* kpages, const void* vpages, const int32_t* block_table,
+                                     int max_pages_per_seq, int page_size, int num_pages, const int32_t* lens,
+                                     const int32_t* q_pos, const void* cos, const void* sin, void* o, void* workspace,
+                                     size_t workspace_bytes, int B, int Hq, int Hkv, int head_dim, int kv_head_begin,
+                                     int kv_head_count, int split_len, float scale, int flags, gqa_stream_t stream) {
+  using namespace decode;
+  if (!q || !kpages || !vpages || !block_table || !lens || !o) return GQA_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || split_len < 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (max_pages_per_seq <= 0 || page_size <= 0 || num_pages <= 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (head_dim != kD || Hq != kG * Hkv) return GQA_ERR_UNSUPPORTED;
+  // chunks of 128 keys must not straddle pages, and splits must start on a chunk
+  if (page_size % 128 || split_len % 128) return GQA_ERR_UNSUPPORTED;
+  const long long capacity = static_cast<long long>(max_pages_per_seq) * page_size;
+  if (capacity > (1LL << 30) || static_cast<long long>(num_pages) * Hkv > (1LL << 31) - 1 || page_size > (1 << 20))
+    return GQA_ERR_UNSUPPORTED;
+  if (kv_head_begin < 0 || kv_head_count <= 0 || kv_head_begin + kv_head_count > Hkv) return GQA_ERR_INVALID_ARGUMENT;
+  if (!(scale > 0.0f) || !(scale < 1e30f)) return GQA_ERR_INVALID_ARGUMENT;
+  if (flags & ~(GQA_FLAG_ROPE_Q)) return GQA_ERR_INVALID_ARGUMENT;
+  if ((flags & GQA_FLAG_ROPE_Q) && (!cos || !sin || !q_pos)) return GQA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q) || !aligned16(kpages) || !aligned16(vpages) || !aligned16(o)) return GQA_ERR_MISALIGNED;
+  const int max_len = static_cast<int>(capacity);
+  const size_t need = gqa_decode_workspace_size(B, Hq, max_len, split_len);
+  if (!workspace || workspace_bytes < need) return GQA_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return GQA_ERR_MISALIGNED;
+  const int sl = effective_split(max_len, split_len);
+  const int ns = (max_len + sl - 1) / sl;
+  if (ns > 65535 || B > 65535) return GQA_ERR_UNSUPPORTED;
+  return launch_decode_tc(q, kpages, vpages, lens, q_pos, cos, sin, o, static_cast<float*>(workspace), B, max_len, Hq,
+                          Hkv, kv_head_begin, kv_head_count, sl, ns, scale, flags, stream, block_table, page_size,
+                          max_pages_per_seq, num_pages);
+}
+
+// ---------------------------------------------------------------------------
 // Allocation-free variant of gqa_decode_bf16.
 //
 // Some callers cannot allocate device memory: a plugin host that hands the

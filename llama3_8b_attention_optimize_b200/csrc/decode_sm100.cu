@@ -63,6 +63,7 @@ enum : int {
   SITE_SOFTMAX = 0x203,
   SITE_DRAIN = 0x204,
   SITE_SMEM_ALIGN = 0x205,
+  SITE_BAD_PAGE = 0x301,  // a block-table entry outside [0, num_pages) (input error)
 };
 
 struct Params {
@@ -74,6 +75,10 @@ struct Params {
   float* ws_o;   // [B][Hq][n_splits][128]
   float* ws_ml;  // [B][Hq][n_splits][2]
   uint16_t* out; // [B][Hq][128]
+  // Paged cache (table != nullptr): K/V pages [num_pages][Hkv][page_size][128]; key j of
+  // sequence b lives in page table[b * max_pages + j / page_size], row j % page_size.
+  const int32_t* table;
+  int page_size, max_pages, num_pages;
   int B, Lmax, Hq, Hkv, kv_begin, kv_count, n_splits, split_len, flags;
   float scale_log2;
 };
@@ -168,14 +173,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long c = 0;  // global chunk counter of this CTA
       for (long long it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
         const Item x = item_of(p, it);
-        const int z = x.b * p.Hkv + x.g;
         for (int ch = 0; ch < x.nchunks; ++ch, ++c) {
           const int s = static_cast<int>(c % kStages);
           const long long r = c / kStages;
           if (r > 0) ok = mbar_wait(bar(B_KVEMPTY + s), static_cast<uint32_t>((r - 1) & 1), SITE_PRODUCER);
           if (!ok) break;
           const uint32_t dst = sbase + kOffKV + s * kStageBytes;
-          const int key0 = x.k0 + ch * kChunk;
+          int key0 = x.k0 + ch * kChunk;
+          int z = x.b * p.Hkv + x.g;
+          if (p.table) {  // 128-key chunks never straddle a page (page_size, split % 128 == 0)
+            int page = __ldg(p.table + static_cast<size_t>(x.b) * p.max_pages + key0 / p.page_size);
+            if (page < 0 || page >= p.num_pages) {
+              record_input_error(SITE_BAD_PAGE);
+              page = 0;  // keep the pipeline flowing; the call reports the input error
+            }
+            z = page * p.Hkv + x.g;
+            key0 %= p.page_size;
+          }
           mbar_expect_tx(bar(B_KVFULL + s), kStageBytes);
           tma_load_3d(dst, &tmK, bar(B_KVFULL + s), 0, key0, z);
           tma_load_3d(dst + kHalfBytes, &tmK, bar(B_KVFULL + s), 64, key0, z);
@@ -185,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // drain: every issued load must land before the CTA exits
       for (long long i = c > kStages ? c - kStages : 0; i < c; ++i)
-        mbar_wait(bar(B_KVFULL + static_cast<int>(i % kStages)), static_cast<uint32_t>((i / kStages) & 1), SITE_DRAIN);
+        mbar_wait_drain(bar(B_KVFULL + static_cast<int>(i % kStages)), static_cast<uint32_t>((i / kStages) & 1), SITE_DRAIN);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -252,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok) flush_pv();
       umma_commit(bar(B_DRAIN));
-      mbar_wait(bar(B_DRAIN), 0, SITE_DRAIN);
+      mbar_wait_drain(bar(B_DRAIN), 0, SITE_DRAIN);
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -460,14 +474,15 @@ __global__ void __launch_bounds__(kD) combine_kernel(const Params p) {
 int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
                      const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,
                      int kv_begin, int kv_count, int split_len, int n_splits, float scale, int flags,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const int32_t* table, int page_size, int max_pages, int num_pages) {
   using namespace decode2;
   CUtensorMap tmK, tmV;
   int rc;
-  if ((rc = make_tmap_3d_bf16(&tmK, kcache, kD, max_len, static_cast<long long>(B) * Hkv, 64, kChunk, 1)) != GQA_OK)
-    return rc;
-  if ((rc = make_tmap_3d_bf16(&tmV, vcache, kD, max_len, static_cast<long long>(B) * Hkv, 64, kChunk, 1)) != GQA_OK)
-    return rc;
+  // contiguous: rows (B*Hkv) x max_len keys; paged: rows (num_pages*Hkv) x page_size keys
+  const int rows_per_z = table ? page_size : max_len;
+  const long long nz = table ? static_cast<long long>(num_pages) * Hkv : static_cast<long long>(B) * Hkv;
+  if ((rc = make_tmap_3d_bf16(&tmK, kcache, kD, rows_per_z, nz, 64, kChunk, 1)) != GQA_OK) return rc;
+  if ((rc = make_tmap_3d_bf16(&tmV, vcache, kD, rows_per_z, nz, 64, kChunk, 1)) != GQA_OK) return rc;
   static std::atomic<uint64_t> attr_done{0};
   if ((rc = ensure_smem_attr(decode_kernel, kSmemBytes, attr_done)) != GQA_OK) return rc;
   int dev = 0, sms = 148;
@@ -483,6 +498,10 @@ int launch_decode_tc(const void* q, const void* kcache, const void* vcache, cons
   p.ws_o = ws;
   p.ws_ml = ws + n_slots * kD;
   p.out = static_cast<uint16_t*>(o);
+  p.table = table;
+  p.page_size = page_size;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
   p.B = B;
   p.Lmax = max_len;
   p.Hq = Hq;

@@ -44,6 +44,7 @@ int error_flag_prefill8(bool clear);
 int error_flag_decode(bool clear);
 int error_flag_decode_tc(bool clear);
 int error_flag_gemm(bool clear);
+int error_flag_kvcache(bool clear);
 
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
@@ -60,6 +61,7 @@ int launch_prefill8(const void* q, const void* k, const void* v, void* o, const 
 int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
                      const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,
                      int kv_begin, int kv_count, int split_len, int n_splits, float scale, int flags,
-                     cudaStream_t stream);
+                     cudaStream_t stream, const int32_t* table = nullptr, int page_size = 0, int max_pages = 0,
+                     int num_pages = 0);
 
 }  // namespace gqa

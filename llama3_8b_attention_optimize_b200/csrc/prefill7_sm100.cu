@@ -248,10 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++uc;
       }
       for (uint32_t i = L > static_cast<uint32_t>(kStages) ? L - kStages : 0u; i < L; ++i)
-        mbar_wait(bar(B_KVFULL + static_cast<int>(i % kStages)), (i / kStages) & 1u, SITE_DRAIN);
+        mbar_wait_drain(bar(B_KVFULL + static_cast<int>(i % kStages)), (i / kStages) & 1u, SITE_DRAIN);
       if (uc > 0) {
-        mbar_wait(bar(B_QFULL + 0), (uc - 1) & 1, SITE_DRAIN);
-        mbar_wait(bar(B_QFULL + 1), (uc - 1) & 1, SITE_DRAIN);
+        mbar_wait_drain(bar(B_QFULL + 0), (uc - 1) & 1, SITE_DRAIN);
+        mbar_wait_drain(bar(B_QFULL + 1), (uc - 1) & 1, SITE_DRAIN);
       }
     }
     __syncwarp();
@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++uc;
       }
       umma_commit(bar(B_DRAIN));
-      mbar_wait(bar(B_DRAIN), 0, SITE_DRAIN);
+      mbar_wait_drain(bar(B_DRAIN), 0, SITE_DRAIN);
     }
     __syncwarp();
   } else if (warp >= kWarpRope0) {

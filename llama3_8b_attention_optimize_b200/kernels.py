@@ -214,6 +214,88 @@ def decode(q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, lens: to
     return out
 
 
+def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+              lens: torch.Tensor, *, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+              block_table: torch.Tensor | None = None, lens_out: torch.Tensor | None = None) -> None:
+    """Write k_new/v_new [B,Hkv,n,128] at positions lens[b] + i of the cache, K rotated
+    there when (cos, sin) are given.  Contiguous cache [B,Hkv,Lmax,128], or (with
+    ``block_table`` int32 [B,max_pages]) page pools [num_pages,Hkv,page_size,128].
+    ``lens_out`` (may be ``lens``) receives lens + n after the writes."""
+    for t, n in ((k_new, "k_new"), (v_new, "v_new"), (kcache, "kcache"), (vcache, "vcache")):
+        _need(t, n)
+    _need(lens, "lens", torch.int32)
+    B, Hkv, n, d = k_new.shape
+    if v_new.shape != k_new.shape or vcache.shape != kcache.shape or lens.shape != (B,):
+        raise ValueError("bad kv_append shapes")
+    flags = 0
+    if cos is not None or sin is not None:
+        _need(cos, "cos")
+        _need(sin, "sin")
+        flags |= GQA_FLAG_ROPE_K
+    if block_table is not None:
+        _need(block_table, "block_table", torch.int32)
+        num_pages, _, page_size, _ = kcache.shape
+        max_pages, max_len = block_table.shape[1], 0
+        if block_table.shape[0] != B or kcache.shape[1] != Hkv:
+            raise ValueError("bad paged kv_append shapes")
+    else:
+        if kcache.shape[:2] != (B, Hkv):
+            raise ValueError("bad kv_append cache shape")
+        num_pages = page_size = max_pages = 0
+        max_len = kcache.shape[2]
+    if lens_out is not None:
+        _need(lens_out, "lens_out", torch.int32)
+    capacity = max_pages * page_size if block_table is not None else max_len
+    if flags and (cos.shape[0] < capacity or sin.shape[0] < capacity):
+        raise ValueError("kv_append rope tables need one row per cache position")
+    check(_lib.load().gqa_kv_append_bf16(_ptr(k_new), _ptr(v_new), _ptr(kcache), _ptr(vcache),
+                                         _ptr(block_table) if block_table is not None else None, max_pages, page_size,
+                                         num_pages, _ptr(lens), _ptr(lens_out) if lens_out is not None else None,
+                                         _ptr(cos) if cos is not None else None, _ptr(sin) if sin is not None else None,
+                                         B, Hkv, n, d, max_len, flags, _stream(k_new.device)), "gqa_kv_append_bf16")
+
+
+def decode_paged(q: torch.Tensor, kpages: torch.Tensor, vpages: torch.Tensor, block_table: torch.Tensor,
+                 lens: torch.Tensor, *, q_pos: torch.Tensor | None = None, cos: torch.Tensor | None = None,
+                 sin: torch.Tensor | None = None, workspace: torch.Tensor | None = None, split_len: int = 0,
+                 scale: float | None = None, kv_heads: tuple[int, int] | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Split-KV decode over page pools kpages/vpages [num_pages,Hkv,page_size,128] with
+    block_table int32 [B,max_pages] (page_size a multiple of 128)."""
+    for t, n in ((q, "q"), (kpages, "kpages"), (vpages, "vpages")):
+        _need(t, n)
+    _need(lens, "lens", torch.int32)
+    _need(block_table, "block_table", torch.int32)
+    B, Hq, d = q.shape
+    num_pages, Hkv, page_size, _ = kpages.shape
+    max_pages = block_table.shape[1]
+    if vpages.shape != kpages.shape or block_table.shape[0] != B or lens.shape != (B,):
+        raise ValueError("bad paged decode shapes")
+    capacity = max_pages * page_size
+    flags = 0
+    if q_pos is not None:
+        _need(q_pos, "q_pos", torch.int32)
+        _need(cos, "cos")
+        _need(sin, "sin")
+        if cos.shape[0] < capacity + 1 or sin.shape[0] < capacity + 1:
+            raise ValueError("decode rope tables need capacity + 1 rows")
+        flags |= GQA_FLAG_ROPE_Q
+    need = decode_workspace_bytes(B, Hq, capacity, split_len)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q) if out is None else out
+    kb, kc = (0, Hkv) if kv_heads is None else kv_heads
+    check(_lib.load().gqa_decode_paged_bf16(_ptr(q), _ptr(kpages), _ptr(vpages), _ptr(block_table), max_pages,
+                                            page_size, num_pages, _ptr(lens),
+                                            _ptr(q_pos) if q_pos is not None else None,
+                                            _ptr(cos) if cos is not None else None,
+                                            _ptr(sin) if sin is not None else None, _ptr(out), _ptr(workspace),
+                                            workspace.numel() * workspace.element_size(), B, Hq, Hkv, d, kb, kc,
+                                            split_len, default_scale(d) if scale is None else float(scale), flags,
+                                            _stream(q.device)), "gqa_decode_paged_bf16")
+    return out
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, *, out_f32: bool = False,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """bf16(x @ w^T) (or the fp32 sums with ``out_f32``) for x [..., K], w [N, K] in the

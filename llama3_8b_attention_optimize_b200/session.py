@@ -158,3 +158,84 @@ class DecodeSession:
         self.run_device(kcache, vcache)
         out_h.copy_(self.o, non_blocking=True)
         return out_h
+
+
+class PagedKVCache:
+    """Paged K/V cache for serving decode: page pools on the device, block tables and a
+    free list of pages kept on the host.
+
+    Pools ``k``/``v`` are [num_pages, Hkv, page_size, 128] bf16; ``table`` int32
+    [B, max_pages_per_seq] maps a sequence's logical page to a pool page (-1 = none);
+    ``lens`` int32 [B] on the device is the number of cached tokens per sequence.
+    ``append`` reserves pages, writes the new rows with K rotated at their positions
+    (``gqa_kv_append_bf16``) and advances ``lens``; ``decode`` runs the split-KV decode
+    over the pages (``gqa_decode_paged_bf16``) with q rotated at its position.
+    """
+
+    def __init__(self, B: int, num_pages: int, max_pages_per_seq: int, Hkv: int = 8, Hq: int = 32,
+                 page_size: int = 128, head_dim: int = 128, *, split_len: int = 0,
+                 theta: float = kernels.ROPE_THETA, device=None):
+        if page_size % 128:
+            raise ValueError("page_size must be a multiple of 128")
+        self.device = torch.device(device or "cuda")
+        self.B, self.Hkv, self.Hq, self.page_size = B, Hkv, Hq, page_size
+        self.max_pages = max_pages_per_seq
+        self.capacity = max_pages_per_seq * page_size
+        self.split_len = split_len
+        shape = (num_pages, Hkv, page_size, head_dim)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        self.table = torch.full((B, max_pages_per_seq), -1, dtype=torch.int32, device=self.device)
+        self.lens = torch.zeros(B, dtype=torch.int32, device=self.device)
+        self._table_h = [[-1] * max_pages_per_seq for _ in range(B)]
+        self._lens_h = [0] * B
+        self._free = list(range(num_pages - 1, -1, -1))
+        self.cos, self.sin = kernels.rope_cache(self.capacity + 1, head_dim, theta, device=self.device)
+        self.ws = torch.empty(max(kernels.decode_workspace_bytes(B, Hq, self.capacity, split_len), 16),
+                              dtype=torch.uint8, device=self.device)
+
+    @property
+    def free_pages(self) -> int:
+        return len(self._free)
+
+    def seq_len(self, b: int) -> int:
+        return self._lens_h[b]
+
+    def reserve(self, n_new: int) -> None:
+        """Give every sequence pages for n_new more tokens (raises when out of pages)."""
+        changed = False
+        for b in range(self.B):
+            need = self._lens_h[b] + n_new
+            if need > self.capacity:
+                raise ValueError(f"sequence {b}: {need} tokens exceed the capacity {self.capacity}")
+            for lp in range((need + self.page_size - 1) // self.page_size):
+                if self._table_h[b][lp] < 0:
+                    if not self._free:
+                        raise RuntimeError("paged KV cache: out of pages")
+                    self._table_h[b][lp] = self._free.pop()
+                    changed = True
+        if changed:
+            self.table.copy_(torch.tensor(self._table_h, dtype=torch.int32))
+
+    def release(self, b: int) -> None:
+        """Return sequence b's pages to the free list and reset its length."""
+        for lp, page in enumerate(self._table_h[b]):
+            if page >= 0:
+                self._free.append(page)
+                self._table_h[b][lp] = -1
+        self._lens_h[b] = 0
+        self.table[b].fill_(-1)
+        self.lens[b] = 0
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
+        """k_new/v_new [B, Hkv, n, 128] (K before RoPE): cached at positions lens[b] + i."""
+        n = k_new.shape[2]
+        self.reserve(n)
+        kernels.kv_append(k_new, v_new, self.k, self.v, self.lens, cos=self.cos, sin=self.sin,
+                          block_table=self.table, lens_out=self.lens)
+        self._lens_h = [x + n for x in self._lens_h]
+
+    def decode(self, q: torch.Tensor, q_pos: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """q [B, Hq, 128] (before RoPE) at positions q_pos (int32 [B]) over the cached tokens."""
+        return kernels.decode_paged(q, self.k, self.v, self.table, self.lens, q_pos=q_pos, cos=self.cos,
+                                    sin=self.sin, workspace=self.ws, split_len=self.split_len, out=out)

@@ -100,3 +100,42 @@ def test_python_wrappers_refuse_cpu_tensors():
     q = torch.zeros(1, 4, 16, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         kernels.prefill(q, q[:, :1], q[:, :1])
+
+
+def test_paged_cache_entry_points_validate_on_host(lib):
+    E = _lib
+    fake = ctypes.c_void_p(0x1000)
+    # decode over pages: page_size / split not multiples of 128, null table, bad head_dim
+    args = dict(max_pages=4, page_size=128, num_pages=8, B=2, Hq=32, Hkv=8, d=128, split=0, flags=0)
+
+    def dec(**kw):
+        a = {**args, **kw}
+        return lib.gqa_decode_paged_bf16(fake, fake, fake, kw.get("table", fake), a["max_pages"], a["page_size"],
+                                         a["num_pages"], fake, None, None, None, fake, fake, 1 << 30, a["B"], a["Hq"],
+                                         a["Hkv"], a["d"], 0, a["Hkv"], a["split"], 0.088, a["flags"], None)
+
+    assert dec(page_size=64) == E.GQA_ERR_UNSUPPORTED
+    assert dec(split=192) == E.GQA_ERR_UNSUPPORTED
+    assert dec(table=None) == E.GQA_ERR_INVALID_ARGUMENT
+    assert dec(d=64) == E.GQA_ERR_UNSUPPORTED
+    assert dec(num_pages=0) == E.GQA_ERR_INVALID_ARGUMENT
+    assert dec(flags=2) == E.GQA_ERR_INVALID_ARGUMENT  # ROPE_Q without tables / q_pos
+    assert dec(flags=4) == E.GQA_ERR_INVALID_ARGUMENT
+
+    def app(**kw):
+        a = dict(table=fake, max_pages=4, page_size=16, num_pages=8, B=2, Hkv=8, n=3, d=128, max_len=0, flags=0)
+        a.update(kw)
+        return lib.gqa_kv_append_bf16(fake, fake, fake, fake, a["table"], a["max_pages"], a["page_size"],
+                                      a["num_pages"], fake, None, None, None, a["B"], a["Hkv"], a["n"], a["d"],
+                                      a["max_len"], a["flags"], None)
+
+    assert app(d=64) == E.GQA_ERR_UNSUPPORTED
+    assert app(n=0) == E.GQA_ERR_INVALID_ARGUMENT
+    assert app(flags=4) == E.GQA_ERR_INVALID_ARGUMENT  # ROPE_K without tables
+    assert app(flags=2) == E.GQA_ERR_INVALID_ARGUMENT
+    assert app(table=None, max_len=0) == E.GQA_ERR_INVALID_ARGUMENT
+    assert app(page_size=0) == E.GQA_ERR_INVALID_ARGUMENT
+    mis = ctypes.c_void_p(0x1002)
+    assert lib.gqa_kv_append_bf16(mis, fake, fake, fake, None, 0, 0, 0, fake, None, None, None, 2, 8, 3, 128, 64, 0,
+                                  None) == E.GQA_ERR_MISALIGNED
+    assert lib.gqa_strerror(E.GQA_ERR_DEVICE_INPUT)
