@@ -282,6 +282,7 @@ def run_ours(args, world, rank, local):
     dec_bytes_rank = float(lens_all.sum().item()) * hkv * D * 2 * 2
     dec_bytes_total = float(lens_all.sum().item()) * HKV * D * 2 * 2
     dec_gbs = dec_bytes_total / (ms_dec * 1e-3) / 1e9
+    paged = run_decode_paged(args, world, dev, stream, ds, kc, vc, lens_all, hkv, dec_bytes_total, ms_dec)
     del kc, vc
 
     # ---- full attention layer (S=4096, hidden 4096): q/k/v projection with RoPE in the
@@ -325,6 +326,7 @@ def run_ours(args, world, rank, local):
         "decode": {"metric": "split-KV GQA decode HBM GB/s", "value": dec_gbs, "unit": "GB/s", "ms_per_step": ms_dec,
                    "config": {"batch": dB, "max_len": DEC_LMAX, "lens": "U[1024,32768] seed 99",
                               "kv_heads_per_gpu": hkv}, "roofline": dec_roof, "gpu_launches": 2 * dsteps},
+        "decode_paged": paged,
         "full_layer": layer,
     }
     lt = layer["achieved_per_gpu"]
@@ -333,6 +335,68 @@ def run_ours(args, world, rank, local):
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return 0
+
+
+def run_decode_paged(args, world, dev, stream, ds, kc, vc, lens_all, hkv, dec_bytes_total, ms_dec) -> dict:
+    """The decode workload over a paged cache: the same rows scattered into shuffled
+    128-key pages (pool sized to the sequences, one spare row each), decoded through the
+    block table; plus the per-step RoPE-on-append of one new token per sequence."""
+    from llama3_8b_attention_optimize_b200 import kernels
+
+    P = 128
+    dB = kc.shape[0]
+    n_lp = [(int(L) + 1 + P - 1) // P for L in lens_all.tolist()]
+    max_pages = max(n_lp)
+    perm = torch.randperm(sum(n_lp), generator=torch.Generator().manual_seed(7)).to(torch.int32)
+    table_h = torch.full((dB, max_pages), -1, dtype=torch.int32)
+    kp = torch.empty(sum(n_lp), hkv, P, D, dtype=torch.bfloat16, device=dev)
+    vp = torch.empty_like(kp)
+    off = 0
+    for b in range(dB):
+        n = n_lp[b]
+        ids = perm[off:off + n]
+        table_h[b, :n] = ids
+        nc = min(n, kc.shape[2] // P)  # a full sequence's spare row lives in a page of its own
+        idx = ids[:nc].to(dev, torch.long)
+        kp[idx] = kc[b, :, :nc * P].reshape(hkv, nc, P, D).transpose(0, 1)
+        vp[idx] = vc[b, :, :nc * P].reshape(hkv, nc, P, D).transpose(0, 1)
+        off += n
+    table = table_h.to(dev)
+    ws = torch.empty(max(kernels.decode_workspace_bytes(dB, ds.Hq, max_pages * P), 16), dtype=torch.uint8,
+                     device=dev)
+    cos, sin = kernels.rope_cache(max_pages * P + 1, device=dev)
+
+    def step():
+        kernels.decode_paged(ds.q, kp, vp, table, ds.lens, q_pos=ds.lens, cos=cos, sin=sin, workspace=ws,
+                             out=ds.o)
+
+    for _ in range(args.warmup):
+        step()
+    ref = ds.run_device(kc, vc).clone()
+    step()
+    kernels.device_check(dev)
+    identical = bool(torch.equal(ds.o, ref))
+    dsteps = max(args.steps, 10)
+    ms = time_loop(step, dsteps, world, stream) / dsteps
+    # one new token per sequence per step: K rotated at lens[b] and written into its page
+    kn = torch.randn(dB, hkv, 1, D, device=dev).to(torch.bfloat16)
+    vn = torch.randn(dB, hkv, 1, D, device=dev).to(torch.bfloat16)
+
+    def app():
+        kernels.kv_append(kn, vn, kp, vp, ds.lens, cos=cos, sin=sin, block_table=table)
+
+    for _ in range(args.warmup):
+        app()
+    ms_app = time_loop(app, dsteps, world, stream) / dsteps
+    kernels.device_check(dev)
+    del kp, vp
+    return {"metric": "paged split-KV GQA decode HBM GB/s", "value": dec_bytes_total / (ms * 1e-3) / 1e9,
+            "unit": "GB/s", "ms_per_step": ms, "vs_contiguous": ms_dec / ms, "bit_identical_to_contiguous": identical,
+            "config": {"page_size": P, "pages": int(sum(n_lp)), "layout": "[pages][kv_heads][128 keys][128]",
+                       "assignment": "shuffled (seed 7)"},
+            "append_us_per_step": ms_app * 1e3,
+            "append_config": "1 token x %d sequences x %d kv heads, RoPE at lens[b], paged" % (dB, hkv),
+            "gpu_launches": 2 * dsteps + dsteps}
 
 
 def run_layer(args, world, rank, dev, stream) -> dict:
