@@ -431,6 +431,28 @@ def run_layer(args, world, rank, dev, stream) -> dict:
         nbytes = ls.partial.numel() * 4
         out["all_reduce"] = {"ms": ar, "bytes": nbytes, "dtype": "fp32",
                              "bus_gbs": nbytes * 2 * (world - 1) / world / (ar * 1e-3) / 1e9}
+        # other ways to combine the row-parallel partials, each checked against the step above:
+        # reduce-scatter fp32 + round + all-gather bf16; o_proj and all-reduce pipelined
+        # over row chunks (GEMM grid capped so NCCL finds free SMs)
+        ls.run_device()
+        ref = ls.out.clone()
+        variants = []
+        for mode, chunks, ctas in (("rs_ag", 1, 0), ("all_reduce", 4, 132), ("all_reduce", 4, 0)):
+            lc = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev, o_chunks=chunks, gemm_ctas=ctas,
+                                  reduce=mode)
+            for dst, src in ((lc.wq, ls.wq), (lc.wk, ls.wk), (lc.wv, ls.wv), (lc.wo, ls.wo), (lc.h, ls.h)):
+                dst.copy_(src)
+            for _ in range(args.warmup):
+                lc.run_device()
+            kernels.device_check(dev)
+            diff = float((lc.out.float() - ref.float()).abs().max().item())
+            msc = time_loop(lc.run_device, lsteps, world, stream) / lsteps
+            kernels.device_check(dev)
+            variants.append({"reduce": mode, "chunks": len(lc.chunks), "gemm_ctas": ctas or "all",
+                             "ms_per_step": msc, "value": fl["total"] / (msc * 1e-3) / 1e12,
+                             "max_abs_diff_vs_all_reduce": diff})
+            del lc
+        out["variants"] = variants
     del ls
     return out
 

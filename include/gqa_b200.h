@@ -215,6 +215,14 @@ int gqa_qkv_proj_bf16(const void* h, const void* wq, const void* wk, const void*
 int gqa_o_proj_bf16(const void* attn, const void* wo, void* out, int B, int S, int Hq, int head_dim, int N, int ldw,
                     int flags, gqa_stream_t stream);
 
+/* Rows [s0, s0 + s_count) of gqa_o_proj_bf16's result for one sequence (B = 1):
+ * attn [Hq][S][128], out [S][N] of which only the chunk's rows are written.  For
+ * overlapping the reduction of finished rows with the next chunk's GEMM (tensor-parallel
+ * o_proj); max_ctas > 0 caps the persistent grid (leaving SMs free for a collective).
+ * Every row is bit-identical to the full call's.                                     */
+int gqa_o_proj_rows_bf16(const void* attn, const void* wo, void* out, int S, int s0, int s_count, int Hq,
+                         int head_dim, int N, int ldw, int max_ctas, int flags, gqa_stream_t stream);
+
 /* dst[i] = bf16_rne(src[i]) for n fp32 values (src 16-byte aligned, dst 8-byte). */
 int gqa_cast_f32_bf16(const void* src, void* dst, long long n, gqa_stream_t stream);
 

@@ -56,6 +56,7 @@ SIGNATURES = {
     "gqa_qkv_proj_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_o_proj_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_cast_f32_bf16": (_i, [_vp, _vp, _ll, _vp]),
+    "gqa_o_proj_rows_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
 }
 
 

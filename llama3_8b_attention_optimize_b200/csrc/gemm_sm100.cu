@@ -363,6 +363,7 @@ struct Launch {
   const void* cos;
   const void* sin;
   int pos0;
+  int max_ctas;  // persistent grid cap (0 = one CTA per SM), e.g. to leave SMs to a collective
 };
 
 template <int BN>
@@ -404,7 +405,8 @@ int launch_bn(const Launch& L, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = p.n_tiles < sms ? p.n_tiles : sms;
+  const int cap = L.max_ctas > 0 && L.max_ctas < sms ? L.max_ctas : sms;
+  const int grid = p.n_tiles < cap ? p.n_tiles : cap;
   gemm_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
@@ -591,6 +593,52 @@ extern "C" int gqa_o_proj_bf16(const void* attn, const void* wo, void* out, int 
   L.c_strides[0][0] = N * esz;
   L.c_strides[0][1] = L.c_strides[0][0] * B * S;
   L.c_strides[0][2] = L.c_strides[0][1];
+  return gemm::launch(L, static_cast<cudaStream_t>(stream));
+}
+
+// Rows [s0, s0 + s_count) of the o_proj output of one sequence (B = 1): attn [Hq][S][128]
+// head-major, out [S][N] (only the chunk's rows written).  Lets a caller overlap the
+// reduction of finished rows with the GEMM of the next ones; max_ctas caps the
+// persistent grid so that a collective running beside it finds free SMs.
+extern "C" int gqa_o_proj_rows_bf16(const void* attn, const void* wo, void* out, int S, int s0, int s_count, int Hq,
+                                    int head_dim, int N, int ldw, int max_ctas, int flags, gqa_stream_t stream) {
+  if (!attn || !wo || !out || S <= 0 || Hq <= 0 || N <= 0 || s_count <= 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (s0 < 0 || s0 + s_count > S || max_ctas < 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (flags & ~GQA_GEMM_OUT_F32) return GQA_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return GQA_ERR_UNSUPPORTED;
+  if (ldw < Hq * 128) return GQA_ERR_INVALID_ARGUMENT;
+  const bool f32 = (flags & GQA_GEMM_OUT_F32) != 0;
+  const long long esz = f32 ? 4 : 2;
+  if (bad16(attn) || bad16(wo) || bad16(out)) return GQA_ERR_MISALIGNED;
+  if (ldw % 8 || (f32 ? N % 4 : N % 8)) return GQA_ERR_MISALIGNED;
+  gemm::Launch L{};
+  L.a = static_cast<const uint16_t*>(attn) + static_cast<size_t>(s0) * 128;  // token s0 of head 0
+  L.a_dims[0] = 128;
+  L.a_dims[1] = s_count;
+  L.a_dims[2] = Hq;
+  L.a_dims[3] = 1;
+  L.a_strides[0] = 256;
+  L.a_strides[1] = 256LL * S;
+  L.a_strides[2] = 256LL * S * Hq;
+  L.a_kin = 128;
+  L.M = s_count;
+  L.N = N;
+  L.K = Hq * 128;
+  L.S = s_count;
+  L.out_f32 = f32 ? 1 : 0;
+  L.n_regions = 1;
+  L.reg[0] = gemm::Region{0, N, 0, 0};
+  L.w[0] = wo;
+  L.ldw[0] = ldw;
+  L.c[0] = static_cast<uint8_t*>(out) + static_cast<size_t>(s0) * N * esz;
+  L.c_dims[0][0] = N;
+  L.c_dims[0][1] = s_count;
+  L.c_dims[0][2] = 1;
+  L.c_dims[0][3] = 1;
+  L.c_strides[0][0] = N * esz;
+  L.c_strides[0][1] = L.c_strides[0][0] * s_count;
+  L.c_strides[0][2] = L.c_strides[0][1];
+  L.max_ctas = max_ctas;
   return gemm::launch(L, static_cast<cudaStream_t>(stream));
 }
 

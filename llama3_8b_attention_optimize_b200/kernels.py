@@ -374,6 +374,31 @@ def o_proj(attn: torch.Tensor, wo: torch.Tensor, *, head_begin: int = 0, out_f32
     return out
 
 
+def o_proj_rows(attn: torch.Tensor, wo: torch.Tensor, out: torch.Tensor, s0: int, s_count: int, *,
+                head_begin: int = 0, out_f32: bool = False, max_ctas: int = 0) -> torch.Tensor:
+    """Rows [s0, s0+s_count) of ``o_proj`` for one sequence: attn [H, S, 128] (or
+    [1, H, S, 128]) into the full-size ``out`` [S, N] (or [1, S, N]); the other rows are
+    left alone.  ``max_ctas`` > 0 caps the GEMM's persistent grid."""
+    _need(attn, "attn")
+    _need(wo, "wo")
+    a4 = _bhsd(attn, "attn")
+    B, H, S, d = a4.shape
+    if B != 1:
+        raise ValueError("o_proj_rows takes one sequence")
+    N, width = wo.shape
+    if (head_begin + H) * d > width:
+        raise ValueError("wo has fewer input columns than the heads need")
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    _need(out, "out", odt)
+    if out.numel() != S * N:
+        raise ValueError("out must hold all S x N rows")
+    w_ptr = _ptr(wo) + head_begin * d * wo.element_size()
+    check(_lib.load().gqa_o_proj_rows_bf16(_ptr(attn), w_ptr, _ptr(out), S, s0, s_count, H, d, N, width, max_ctas,
+                                           GQA_GEMM_OUT_F32 if out_f32 else 0, _stream(attn.device)),
+          "gqa_o_proj_rows_bf16")
+    return out
+
+
 def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Round an fp32 tensor to bf16 (RNE), e.g. all-reduced o_proj partials."""
     _need(x, "x", torch.float32)

@@ -11,8 +11,17 @@ Per step, on every rank (rank r owns kv heads [g0, g0+c) and q heads [4g0, 4(g0+
   4. all-reduce (sum)    NCCL over NVLink / NVSwitch (world > 1 only)
   5. gqa_cast_f32_bf16   one rounding of the summed partials (world > 1 only)
 
+``reduce="rs_ag"`` replaces 4-5 by a reduce-scatter of the fp32 partials (each rank sums
+S/world rows), the rounding of those rows, and an all-gather of the bf16 rows: the same
+one rounding of the fp32 sum, with 3/4 of the all-reduce's bytes on the links.
+
 With one GPU, step 3 writes the bf16 output directly and 4-5 are skipped.  Summing
 fp32 partials and rounding once keeps the single bf16 rounding of :194.
+
+With ``o_chunks`` > 1 (one sequence), steps 3-5 run as a pipeline over row chunks: the
+GEMM of chunk i+1 (on the compute stream, grid capped to leave SMs for NCCL) overlaps the
+all-reduce and the rounding of chunk i (on a communication stream).  Every row is
+computed exactly as in the unchunked step.
 """
 from __future__ import annotations
 
@@ -50,12 +59,75 @@ def reduce_partials(partial: torch.Tensor, world: int, group=None) -> torch.Tens
     return partial
 
 
+def row_chunks(S: int, n_chunks: int, align: int = 128) -> list:
+    """Split rows [0, S) into up to n_chunks contiguous (s0, count) ranges whose starts are
+    multiples of ``align`` (GEMM tile rows), as even as that allows."""
+    if S <= 0 or n_chunks <= 0:
+        raise ValueError("row_chunks needs S > 0 and n_chunks > 0")
+    tiles = (S + align - 1) // align
+    n = min(n_chunks, tiles)
+    bounds = [min(S, ((i * tiles) // n) * align) for i in range(n)] + [S]
+    return [(bounds[i], bounds[i + 1] - bounds[i]) for i in range(n) if bounds[i + 1] > bounds[i]]
+
+
+def reduce_cast_gather(partial: torch.Tensor, out: torch.Tensor, world: int, group=None,
+                       mine: torch.Tensor | None = None, cast=None) -> torch.Tensor:
+    """out = bf16(sum over ranks of partial) via reduce-scatter (fp32 rows [S/world] per
+    rank), the rounding of this rank's rows and an all-gather of the bf16 rows.
+    partial [..., N] fp32 and out [..., N] bf16, the leading dimensions flattened to rows
+    (a multiple of the world size); ``cast`` rounds
+    fp32 -> bf16 (default: torch's round-to-nearest-even)."""
+    import torch.distributed as dist
+
+    n = partial.shape[-1]
+    rows = partial.numel() // n  # all leading dimensions are rows
+    if rows % world:
+        raise ValueError("reduce_cast_gather needs rows divisible by the world size")
+    p2 = partial.reshape(rows, n)
+    o2 = out.reshape(rows, n)
+    if mine is None:
+        mine = torch.empty(rows // world, p2.shape[1], dtype=partial.dtype, device=partial.device)
+    dist.reduce_scatter_tensor(mine, p2, op=dist.ReduceOp.SUM, group=group)
+    mine_bf = cast(mine) if cast is not None else mine.to(out.dtype)
+    dist.all_gather_into_tensor(o2, mine_bf, group=group)
+    return out
+
+
+def pipelined_row_reduce(partial: torch.Tensor, chunks: list, compute, world: int, group=None, finish=None,
+                         comm_stream=None) -> torch.Tensor:
+    """For each row chunk: compute(s0, n) fills partial[s0:s0+n] on the current stream;
+    the chunk is then summed across ranks (all-reduce) and passed to finish(s0, n) on
+    ``comm_stream`` (when given, a CUDA stream that runs beside the next compute).  All
+    ranks issue the same collectives in the same order.  Returns ``partial``."""
+    import torch.distributed as dist
+
+    cur = torch.cuda.current_stream(partial.device) if partial.is_cuda else None
+    for s0, n in chunks:
+        compute(s0, n)
+        rows = partial.narrow(0, s0, n)
+        if comm_stream is not None:
+            comm_stream.wait_stream(cur)
+            with torch.cuda.stream(comm_stream):
+                if world > 1:
+                    dist.all_reduce(rows, op=dist.ReduceOp.SUM, group=group)
+                if finish is not None:
+                    finish(s0, n)
+        else:
+            if world > 1:
+                dist.all_reduce(rows, op=dist.ReduceOp.SUM, group=group)
+            if finish is not None:
+                finish(s0, n)
+    if comm_stream is not None:
+        cur.wait_stream(comm_stream)
+    return partial
+
+
 class FullLayerSession:
     """Device buffers, weight shards and RoPE tables of one attention layer for one shape."""
 
     def __init__(self, S: int, *, B: int = 1, hidden: int = 4096, num_q_heads: int = 32, num_kv_heads: int = 8,
                  head_dim: int = 128, theta: float = kernels.ROPE_THETA, rank: int = 0, world: int = 1, group=None,
-                 device=None):
+                 device=None, o_chunks: int = 1, gemm_ctas: int = 0, reduce: str = "all_reduce"):
         self.device = torch.device(device or "cuda")
         self.shard = kv_shard(rank, world, num_kv_heads, num_q_heads)
         self.world, self.group = world, group
@@ -71,6 +143,16 @@ class FullLayerSession:
         self.partial = mk(B, S, hidden, dt=torch.float32) if world > 1 else None
         self.out = mk(B, S, hidden)
         self.cos, self.sin = kernels.rope_cache(S, head_dim, theta, device=self.device)
+        # o_proj / all-reduce pipeline (one sequence, several ranks)
+        self.o_chunks = o_chunks if (world > 1 and B == 1) else 1
+        self.gemm_ctas = gemm_ctas
+        self.chunks = row_chunks(S, self.o_chunks)
+        self.comm_stream = torch.cuda.Stream(self.device) if self.o_chunks > 1 else None
+        if reduce not in ("all_reduce", "rs_ag"):
+            raise ValueError("reduce must be 'all_reduce' or 'rs_ag'")
+        self.reduce = reduce if (world > 1 and (B * S) % world == 0) else "all_reduce"
+        self._mine = (mk(B * S // world, hidden, dt=torch.float32) if self.reduce == "rs_ag" else None)
+        self._mine_bf = (mk(B * S // world, hidden) if self.reduce == "rs_ag" else None)
 
     def set_weights(self, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, wo: torch.Tensor) -> None:
         """Full HF-layout weights (any device); this rank keeps its shard's slices."""
@@ -78,7 +160,9 @@ class FullLayerSession:
             dst.copy_(src)
 
     def launches_per_step(self) -> int:
-        return 3 if self.world == 1 else 4  # + the NCCL all-reduce kernel (not ours)
+        if self.world == 1:
+            return 3
+        return 2 + 2 * len(self.chunks)  # o_proj and cast per chunk (+ NCCL all-reduces, not ours)
 
     def flops(self) -> dict:
         return layer_flops(self.B, self.S, self.hidden, self.num_q_heads, self.num_kv_heads, self.d)
@@ -99,8 +183,24 @@ class FullLayerSession:
         if self.world == 1:
             self._core()
             return kernels.o_proj(self.attn, self.wo, out=self.out)
-        reduce_partials(self.run_partial(), self.world, self.group)
-        return kernels.cast_bf16(self.partial, out=self.out)
+        if self.reduce == "rs_ag":
+            self.run_partial()
+            return reduce_cast_gather(self.partial, self.out, self.world, self.group, mine=self._mine,
+                                      cast=lambda x: kernels.cast_bf16(x, out=self._mine_bf))
+        if self.o_chunks == 1:
+            reduce_partials(self.run_partial(), self.world, self.group)
+            return kernels.cast_bf16(self.partial, out=self.out)
+        self._core()
+        part, out = self.partial[0], self.out[0]
+
+        def compute(s0, n):
+            kernels.o_proj_rows(self.attn[0], self.wo, part, s0, n, out_f32=True, max_ctas=self.gemm_ctas)
+
+        def finish(s0, n):
+            kernels.cast_bf16(part.narrow(0, s0, n), out=out.narrow(0, s0, n))
+
+        pipelined_row_reduce(part, self.chunks, compute, self.world, self.group, finish, self.comm_stream)
+        return self.out
 
     def run_host(self, h_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
         """h_host [B,S,hidden] / out_host [B,S,hidden]: bf16 CPU tensors (pinned for async copies)."""

@@ -139,3 +139,14 @@ def test_paged_cache_entry_points_validate_on_host(lib):
     assert lib.gqa_kv_append_bf16(mis, fake, fake, fake, None, 0, 0, 0, fake, None, None, None, 2, 8, 3, 128, 64, 0,
                                   None) == E.GQA_ERR_MISALIGNED
     assert lib.gqa_strerror(E.GQA_ERR_DEVICE_INPUT)
+
+
+def test_row_chunks_cover_rows_on_tile_boundaries():
+    from llama3_8b_attention_optimize_b200.layer import row_chunks
+    for S, n in [(4096, 4), (4096, 3), (300, 8), (128, 5), (1, 2), (4097, 4)]:
+        ch = row_chunks(S, n)
+        assert ch[0][0] == 0 and sum(c for _, c in ch) == S and len(ch) <= n
+        assert all(a + c == b for (a, c), (b, _) in zip(ch, ch[1:]))
+        assert all(s0 % 128 == 0 and c > 0 for s0, c in ch)
+    with pytest.raises(ValueError):
+        row_chunks(0, 2)

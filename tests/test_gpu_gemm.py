@@ -232,3 +232,26 @@ def test_layer_session_matches_facade_and_shards_sum():
     kernels.device_check()
     attn = sess.attn[0].transpose(0, 1).contiguous().view(S, -1)
     _check_bf16(total[0], _exact(attn, ws[3]))
+
+
+def test_o_proj_rows_chunks_equal_full_call():
+    """Row chunks of o_proj (the overlap pipeline's GEMM) are bit-identical to the full call,
+    with and without a grid cap, in fp32 and bf16."""
+    g0 = torch.Generator(device="cuda").manual_seed(77)
+    Hq, S, N = 8, 700, 4096
+    attn = (torch.randn(Hq, S, 128, generator=g0, device="cuda")).to(torch.bfloat16)
+    wo = (torch.randn(N, 4096, generator=g0, device="cuda") * 0.02).to(torch.bfloat16)
+    for f32 in (True, False):
+        full = kernels.o_proj(attn, wo, head_begin=2, out_f32=f32)
+        dt = torch.float32 if f32 else torch.bfloat16
+        got = torch.full((S, N), float("nan"), dtype=dt, device="cuda")
+        for (s0, n), cap in zip([(0, 128), (128, 384), (512, 188)], (0, 100, 7)):
+            kernels.o_proj_rows(attn, wo, got, s0, n, head_begin=2, out_f32=f32, max_ctas=cap)
+        kernels.device_check()
+        assert torch.equal(got, full)
+    # a chunk leaves the other rows untouched
+    part = torch.full((S, N), 5.0, dtype=torch.float32, device="cuda")
+    kernels.o_proj_rows(attn, wo, part, 256, 128, out_f32=True)
+    kernels.device_check()
+    assert torch.all(part[:256] == 5.0) and torch.all(part[384:] == 5.0)
+    assert torch.equal(part[256:384], kernels.o_proj(attn, wo, out_f32=True)[256:384])

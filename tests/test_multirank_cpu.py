@@ -26,7 +26,8 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
     sys.path.insert(0, ROOT)
     from datetime import timedelta
 
-    from llama3_8b_attention_optimize_b200.layer import reduce_partials, shard_weights
+    from llama3_8b_attention_optimize_b200.layer import pipelined_row_reduce, reduce_cast_gather, reduce_partials, \
+        row_chunks, shard_weights
     from llama3_8b_attention_optimize_b200.shard import kv_shard
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -56,6 +57,42 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
         reduce_partials(partial, world)
         full = attn.transpose(0, 1).reshape(S, -1).double() @ wo.double().t()
         assert torch.allclose(partial, full, rtol=1e-10, atol=1e-8)
+
+        # 2b. the same reduction pipelined over row chunks (compute chunk, all-reduce it,
+        # finish it), with the chunk boundaries on 128-row tiles: identical sums
+        S2 = 300
+        attn2 = torch.randn(32, S2, d, generator=g)
+        local2 = attn2[sh.q_begin:sh.q_begin + sh.q_count].transpose(0, 1).reshape(S2, -1).double()
+        chunks = row_chunks(S2, 4)
+        # (row blocks multiplied separately: BLAS may block a different M differently)
+        whole = torch.cat([local2[s0:s0 + n] @ swo.double().t() for s0, n in chunks])
+        reduce_partials(whole, world)
+        assert [c[0] for c in chunks] == [0, 128, 256] and sum(c[1] for c in chunks) == S2
+        part = torch.full((S2, hidden), float("nan"), dtype=torch.float64)
+        out = torch.full_like(part, float("nan"))
+        order = []
+
+        def compute(s0, n):
+            order.append(("c", s0))
+            part[s0:s0 + n] = local2[s0:s0 + n] @ swo.double().t()
+
+        def finish(s0, n):
+            order.append(("f", s0))
+            out[s0:s0 + n] = part[s0:s0 + n]
+
+        pipelined_row_reduce(part, chunks, compute, world, finish=finish)
+        assert torch.equal(out, whole) and torch.equal(part, whole)
+        assert order == [("c", 0), ("f", 0), ("c", 128), ("f", 128), ("c", 256), ("f", 256)]
+
+        # 2c. reduce-scatter + round + all-gather == all-reduce then round (fp32 partials)
+        pf = (local2[:256] @ swo.double().t()).float()
+        ar = pf.clone()
+        reduce_partials(ar, world)
+        got = torch.empty(256, hidden, dtype=torch.bfloat16)
+        reduce_cast_gather(pf, got, world)
+        assert torch.equal(got, ar.to(torch.bfloat16))
+        with pytest.raises(ValueError):
+            reduce_cast_gather(pf[:255], got[:255], world)
 
         # 3. bench timing: the slowest rank's time is reported by every rank
         import bench
