@@ -437,9 +437,13 @@ def run_layer(args, world, rank, dev, stream) -> dict:
         ls.run_device()
         ref = ls.out.clone()
         variants = []
-        for mode, chunks, ctas in (("rs_ag", 1, 0), ("all_reduce", 4, 132), ("all_reduce", 4, 0)):
-            lc = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev, o_chunks=chunks, gemm_ctas=ctas,
-                                  reduce=mode)
+        for mode, chunks, ctas in (("p2p", 1, 0), ("rs_ag", 1, 0), ("all_reduce", 4, 132)):
+            try:  # raised on every rank together when peer mapping is unavailable
+                lc = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev, o_chunks=chunks, gemm_ctas=ctas,
+                                      reduce=mode)
+            except RuntimeError as exc:
+                variants.append({"reduce": mode, "unavailable": str(exc)[:200]})
+                continue
             for dst, src in ((lc.wq, ls.wq), (lc.wk, ls.wk), (lc.wv, ls.wv), (lc.wo, ls.wo), (lc.h, ls.h)):
                 dst.copy_(src)
             for _ in range(args.warmup):
@@ -451,6 +455,11 @@ def run_layer(args, world, rank, dev, stream) -> dict:
             variants.append({"reduce": mode, "chunks": len(lc.chunks), "gemm_ctas": ctas or "all",
                              "ms_per_step": msc, "value": fl["total"] / (msc * 1e-3) / 1e12,
                              "max_abs_diff_vs_all_reduce": diff})
+            if mode == "p2p":  # the exchange alone, on a partial already in the buffer
+                lc.peer.reduce_gather()
+                variants[-1]["exchange_ms"] = time_loop(lc.peer.reduce_gather, lsteps, world, stream) / lsteps
+                kernels.device_check(dev)
+            lc.close()
             del lc
         out["variants"] = variants
     del ls

@@ -149,6 +149,31 @@ int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const void* vcach
                             int Hq, int Hkv, int head_dim, int kv_head_begin, int kv_head_count, int split_len,
                             float scale, int flags, gqa_stream_t stream);
 
+/* ---------------------------------------------------------------- tensor-parallel o_proj over NVLink
+ * The row-parallel o_proj leaves each rank an fp32 partial of the same [S][N] output; the
+ * layer output is bf16(sum over ranks), the reference's single rounding (:193-194).
+ * Instead of an NCCL all-reduce, ranks exchange through CUDA IPC peer memory:
+ *  - gqa_tp_buffer_bytes(S, N) bytes per rank, allocated with gqa_peer_alloc (the one
+ *    device allocation this library makes: IPC needs a cudaMalloc base) and laid out as
+ *    [partial fp32 S x N][out bf16 S x N][flags]; its handle (gqa_peer_handle_bytes()
+ *    bytes) goes to every other rank, which maps it with gqa_peer_open;
+ *  - each step the caller writes its partial (e.g. gqa_o_proj_bf16 with
+ *    GQA_GEMM_OUT_F32 into the buffer's start), then calls gqa_tp_reduce_gather_bf16
+ *    with bases[r] = rank r's buffer as mapped in this process (its own for r = rank)
+ *    and an epoch that increases by one per step (starting at 1, the same on every
+ *    rank).  It sums its S/world-row block over all ranks by P2P loads in rank order,
+ *    rounds once, and gathers the other blocks: the buffer's out holds the full bf16
+ *    result when the stream reaches that point.  S % world == 0, N % 8 == 0, world <= 8.
+ * Waits on peers are bounded; a missing peer is reported by gqa_device_check.         */
+size_t gqa_tp_buffer_bytes(int S, int N);
+size_t gqa_peer_handle_bytes(void);
+int gqa_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+int gqa_peer_open(const void* ipc_handle, void** peer_ptr);
+int gqa_peer_close(void* peer_ptr);
+int gqa_peer_free(void* dev_ptr);
+int gqa_tp_reduce_gather_bf16(const void* const* bases, int world, int rank, int S, int N, unsigned int epoch,
+                              gqa_stream_t stream);
+
 /* ---------------------------------------------------------------- paged K/V cache
  * The step after decode (the reference has no serving cache): append each step's new
  * K/V rows to the cache, rotating K at its position, and decode over a paged cache.

@@ -56,6 +56,13 @@ SIGNATURES = {
     "gqa_qkv_proj_bf16": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_o_proj_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gqa_cast_f32_bf16": (_i, [_vp, _vp, _ll, _vp]),
+    "gqa_tp_buffer_bytes": (_sz, [_i, _i]),
+    "gqa_peer_handle_bytes": (_sz, []),
+    "gqa_peer_alloc": (_i, [_sz, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "gqa_peer_open": (_i, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "gqa_peer_close": (_i, [_vp]),
+    "gqa_peer_free": (_i, [_vp]),
+    "gqa_tp_reduce_gather_bf16": (_i, [ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, ctypes.c_uint, _vp]),
     "gqa_o_proj_rows_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
 }
 

@@ -90,7 +90,8 @@ extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   if (site) *site = 0;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return GQA_ERR_CUDA;
   int (*const readers[])(bool) = {error_flag_stages,   error_flag_prefill,   error_flag_prefill7, error_flag_prefill8,
-                                   error_flag_decode, error_flag_decode_tc, error_flag_gemm,     error_flag_kvcache};
+                                   error_flag_decode, error_flag_decode_tc, error_flag_gemm,     error_flag_kvcache,
+                                   error_flag_peer};
   int first = 0;
   for (auto rd : readers) {  // read and clear every file's word; report the first set one
     const int v = rd(true);

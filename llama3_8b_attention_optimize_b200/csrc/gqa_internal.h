@@ -45,6 +45,7 @@ int error_flag_decode(bool clear);
 int error_flag_decode_tc(bool clear);
 int error_flag_gemm(bool clear);
 int error_flag_kvcache(bool clear);
+int error_flag_peer(bool clear);
 
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,

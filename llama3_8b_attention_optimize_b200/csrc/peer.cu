@@ -1,0 +1,270 @@
+// peer.cu -- tensor-parallel o_proj reduction over NVLink peer memory (no NCCL).
+//
+// Row-parallel o_proj leaves every rank with an fp32 partial [S][N] of the same output;
+// the layer's result is bf16(sum over ranks).  Each rank exports one buffer
+//   [partial fp32 S x N][out bf16 S x N][flags]
+// through CUDA IPC and maps its peers' buffers.  One step (epoch e) is three launches per
+// rank after the o_proj GEMM has written the local partial:
+//   1. signal: raise this rank's "partial ready" flag to e;
+//   2. tp_reduce: wait until every rank's "partial ready" flag is e, then sum the rank's
+//      own row block of all partials in rank order by P2P loads over NVLink, round once
+//      to bf16, store into the local out; the last block to finish raises this rank's
+//      "block done" flag to e;
+//   3. tp_gather: wait until every rank's "block done" flag is e, then copy the other
+//      ranks' bf16 row blocks from their out buffers (P2P loads) into the local out.
+// Flags are raised with a system-scope release after a system-scope fence and read with
+// system-scope acquire loads; every wait is bounded (2 s) and records an error site.
+// Ordering across steps: a rank starts the next step's GEMM (overwriting its partial)
+// only after its gather of this step saw every owner's "done" flag, i.e. after every
+// owner finished reading its partial; an owner overwrites its out block only after every
+// rank raised the next "ready" flag, i.e. after every rank finished its gather.
+// The waiting kernels run on different GPUs (one rank per GPU), never two on one GPU.
+#include <cstring>
+
+#include "common.cuh"
+#include "gqa_internal.h"
+
+namespace gqa {
+namespace peer {
+
+constexpr int kMaxRanks = 8;
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+enum : int {
+  SITE_READY = 0x401,
+  SITE_DONE = 0x402,
+};
+
+struct Ptrs {
+  const float* partial[kMaxRanks];  // each rank's fp32 partial [S][N]
+  const uint16_t* out[kMaxRanks];   // each rank's bf16 out [S][N]
+  uint32_t* ready[kMaxRanks];       // each rank's "partial ready" flag
+  uint32_t* done[kMaxRanks];        // each rank's "block done" flag
+};
+
+struct Params {
+  Ptrs p;
+  uint16_t* out_local;
+  uint32_t* counter;  // local arrival counter of tp_reduce's blocks (zero between launches)
+  int world, rank, S, N;
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// Bounded wait until *flag (a peer's or our own) reaches epoch (flags only increase).
+__device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, int site) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if ((it & 255u) == 255u) {
+      if (error_pending()) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        record_error(site);
+        return false;
+      }
+    }
+  }
+}
+
+// This rank's partial (written by the preceding GEMM launch) is ready.
+__global__ void signal_kernel(uint32_t* flag, uint32_t epoch) {
+  __threadfence_system();
+  st_release_sys(flag, epoch);
+}
+
+__global__ void __launch_bounds__(kThreads) tp_reduce_kernel(const Params prm) {
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int r = 0; r < prm.world && ok; ++r) ok = wait_flag(prm.p.ready[r], prm.epoch, SITE_READY);
+    ok_s = ok ? 1 : 0;
+  }
+  __syncthreads();
+  const int rows = prm.S / prm.world;
+  const long long n4 = static_cast<long long>(rows) * prm.N / 4;  // float4 units of the block
+  const long long base = static_cast<long long>(prm.rank) * rows * prm.N;
+  if (ok_s) {
+    // kUnroll independent float4 units per thread per round, all loads issued before the
+    // adds: remote (NVLink) loads need many bytes in flight
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i0 < n4;
+         i0 += kUnroll * stride) {
+      float4 acc[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const long long i = i0 + u * stride;
+        // peer data is read past L1 (__ldcg): it changes between launches
+        acc[u] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(prm.p.partial[0] + base) + i)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int r = 1; r < prm.world; ++r) {  // rank order: the same sums on every owner
+        float4 x[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const long long i = i0 + u * stride;
+          x[u] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(prm.p.partial[r] + base) + i)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          acc[u].x += x[u].x;
+          acc[u].y += x[u].y;
+          acc[u].z += x[u].z;
+          acc[u].w += x[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const long long i = i0 + u * stride;
+        if (i < n4) {
+          uint2 w;
+          w.x = static_cast<uint32_t>(f2bf_bits(acc[u].x)) | (static_cast<uint32_t>(f2bf_bits(acc[u].y)) << 16);
+          w.y = static_cast<uint32_t>(f2bf_bits(acc[u].z)) | (static_cast<uint32_t>(f2bf_bits(acc[u].w)) << 16);
+          reinterpret_cast<uint2*>(prm.out_local + base)[i] = w;
+        }
+      }
+    }
+  }
+  // the last block to finish announces this rank's block (all blocks' stores fenced first)
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t arrived = atomicAdd(prm.counter, 1u) + 1u;
+    if (arrived == gridDim.x) {
+      *prm.counter = 0u;
+      __threadfence_system();
+      if (ok_s) st_release_sys(prm.p.done[prm.rank], prm.epoch);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) tp_gather_kernel(const Params prm) {
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int r = 0; r < prm.world && ok; ++r) ok = wait_flag(prm.p.done[r], prm.epoch, SITE_DONE);
+    ok_s = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int rows = prm.S / prm.world;
+  const long long blk16 = static_cast<long long>(rows) * prm.N * 2 / 16;  // uint4 units per block
+  const long long total = blk16 * (prm.world - 1);
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i0 < total;
+       i0 += kUnroll * stride) {
+    uint4 v[kUnroll];
+    long long dst[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = i0 + u * stride;
+      dst[u] = -1;
+      if (i < total) {
+        int q = static_cast<int>(i / blk16);
+        q += (q >= prm.rank);  // the other ranks' blocks
+        const long long off = static_cast<long long>(q) * blk16 + i % blk16;
+        v[u] = __ldcg(reinterpret_cast<const uint4*>(prm.p.out[q]) + off);
+        dst[u] = off;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (dst[u] >= 0) reinterpret_cast<uint4*>(prm.out_local)[dst[u]] = v[u];
+  }
+}
+
+}  // namespace peer
+
+GQA_ERROR_FLAG_ACCESSOR(error_flag_peer)
+
+}  // namespace gqa
+
+// ------------------------------------------------------------------ C ABI
+extern "C" int gqa_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return GQA_ERR_INVALID_ARGUMENT;
+  *dev_ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return GQA_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return GQA_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return GQA_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return GQA_OK;
+}
+
+extern "C" size_t gqa_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int gqa_peer_open(const void* ipc_handle, void** peer_ptr) {
+  if (!ipc_handle || !peer_ptr) return GQA_ERR_INVALID_ARGUMENT;
+  *peer_ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+extern "C" int gqa_peer_close(void* peer_ptr) {
+  if (!peer_ptr) return GQA_ERR_INVALID_ARGUMENT;
+  return cudaIpcCloseMemHandle(peer_ptr) == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+extern "C" int gqa_peer_free(void* dev_ptr) {
+  if (!dev_ptr) return GQA_ERR_INVALID_ARGUMENT;
+  return cudaFree(dev_ptr) == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+extern "C" int gqa_tp_reduce_gather_bf16(const void* const* bases, int world, int rank, int S, int N,
+                                         unsigned int epoch, gqa_stream_t stream) {
+  using namespace gqa;
+  using namespace gqa::peer;
+  if (!bases || world < 2 || world > kMaxRanks || rank < 0 || rank >= world) return GQA_ERR_INVALID_ARGUMENT;
+  if (S <= 0 || N <= 0 || S % world || N % 8 || epoch == 0) return GQA_ERR_INVALID_ARGUMENT;
+  Params prm{};
+  const size_t part_bytes = static_cast<size_t>(S) * N * 4, out_bytes = static_cast<size_t>(S) * N * 2;
+  for (int r = 0; r < world; ++r) {
+    const uint8_t* b = static_cast<const uint8_t*>(bases[r]);
+    if (!b || (reinterpret_cast<uintptr_t>(b) & 255u)) return GQA_ERR_MISALIGNED;
+    prm.p.partial[r] = reinterpret_cast<const float*>(b);
+    prm.p.out[r] = reinterpret_cast<const uint16_t*>(b + part_bytes);
+    prm.p.ready[r] = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(b + part_bytes + out_bytes));
+    prm.p.done[r] = prm.p.ready[r] + 1;
+  }
+  prm.out_local = const_cast<uint16_t*>(prm.p.out[rank]);
+  prm.counter = prm.p.ready[rank] + 2;
+  prm.world = world;
+  prm.rank = rank;
+  prm.S = S;
+  prm.N = N;
+  prm.epoch = epoch;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  signal_kernel<<<1, 1, 0, st>>>(prm.p.ready[rank], epoch);
+  if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
+  tp_reduce_kernel<<<2 * sms, kThreads, 0, st>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
+  tp_gather_kernel<<<2 * sms, kThreads, 0, st>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+// [partial fp32 S x N][out bf16 S x N][ready u32][done u32][block counter u32] (+ pad)
+extern "C" size_t gqa_tp_buffer_bytes(int S, int N) {
+  if (S <= 0 || N <= 0) return 0;
+  return static_cast<size_t>(S) * N * 6 + 256;
+}

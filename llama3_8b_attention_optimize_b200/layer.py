@@ -11,6 +11,11 @@ Per step, on every rank (rank r owns kv heads [g0, g0+c) and q heads [4g0, 4(g0+
   4. all-reduce (sum)    NCCL over NVLink / NVSwitch (world > 1 only)
   5. gqa_cast_f32_bf16   one rounding of the summed partials (world > 1 only)
 
+``reduce="p2p"`` replaces 4-5 by an exchange through NVLink peer memory (no NCCL in the
+step): the o_proj partial goes straight into a CUDA-IPC buffer every rank maps
+(``PeerExchange``), each rank sums its row block of all partials by P2P loads, rounds
+once and gathers the other blocks (``gqa_tp_reduce_gather_bf16``).
+
 ``reduce="rs_ag"`` replaces 4-5 by a reduce-scatter of the fp32 partials (each rank sums
 S/world rows), the rounding of those rows, and an all-gather of the bf16 rows: the same
 one rounding of the fp32 sum, with 3/4 of the all-reduce's bytes on the links.
@@ -93,6 +98,94 @@ def reduce_cast_gather(partial: torch.Tensor, out: torch.Tensor, world: int, gro
     return out
 
 
+class _DevArray:
+    """A raw device allocation seen as a torch tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """One CUDA-IPC buffer per rank ([partial fp32 S x N][out bf16 S x N][flags]) mapped by
+    every other rank, for the NVLink-peer reduction of row-parallel partials.
+
+    Construction is collective (handles travel by ``all_gather_object`` on ``group``);
+    ``close()`` is collective too (a barrier, so no rank frees memory a peer still reads).
+    """
+
+    def __init__(self, S: int, N: int, rank: int, world: int, group=None, device=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        lib = _lib.load()
+        self.lib, self.S, self.N, self.rank, self.world, self.group = lib, S, N, rank, world, group
+        self.device = torch.device(device or "cuda")
+        nbytes = lib.gqa_tp_buffer_bytes(S, N)
+        hb = lib.gqa_peer_handle_bytes()
+        handle = ctypes.create_string_buffer(hb)
+        ptr = ctypes.c_void_p()
+        kernels.check(lib.gqa_peer_alloc(nbytes, ctypes.byref(ptr), handle), "gqa_peer_alloc")
+        self._own = ptr.value
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        bases = []
+        err = ""
+        for r, h in enumerate(handles):
+            if r == rank:
+                bases.append(self._own)
+                continue
+            pp = ctypes.c_void_p()
+            rc = lib.gqa_peer_open(ctypes.create_string_buffer(h, hb), ctypes.byref(pp))
+            if rc != 0:
+                err = f"rank {rank}: gqa_peer_open of rank {r}'s buffer failed ({rc})"
+                break
+            self._opened.append(pp.value)
+            bases.append(pp.value)
+        # every rank learns whether every rank could map every peer, so all raise together
+        errs = [None] * world
+        dist.all_gather_object(errs, err, group=group)
+        if any(errs):
+            for pp in self._opened:
+                lib.gqa_peer_close(pp)
+            dist.barrier(group=group)
+            lib.gqa_peer_free(self._own)
+            raise RuntimeError("peer exchange unavailable: " + "; ".join(e for e in errs if e))
+        self._bases = (ctypes.c_void_p * world)(*bases)
+        self.partial = torch.as_tensor(_DevArray(self._own, (S, N), "<f4"), device=self.device)
+        self.out = torch.as_tensor(_DevArray(self._own + S * N * 4, (S, N), "<i2"),
+                                   device=self.device).view(torch.bfloat16)
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def reduce_gather(self) -> torch.Tensor:
+        """Sum the ranks' partials (the caller has written this rank's into ``partial``),
+        round once, and return the full bf16 result in ``out``."""
+        self.epoch += 1
+        kernels.check(self.lib.gqa_tp_reduce_gather_bf16(self._bases, self.world, self.rank, self.S, self.N,
+                                                         self.epoch, kernels._stream(self.device)),
+                      "gqa_tp_reduce_gather_bf16")
+        return self.out
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every rank is done reading every buffer
+        for pp in self._opened:
+            self.lib.gqa_peer_close(pp)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.lib.gqa_peer_free(self._own)
+        self._own = None
+
+
 def pipelined_row_reduce(partial: torch.Tensor, chunks: list, compute, world: int, group=None, finish=None,
                          comm_stream=None) -> torch.Tensor:
     """For each row chunk: compute(s0, n) fills partial[s0:s0+n] on the current stream;
@@ -148,9 +241,15 @@ class FullLayerSession:
         self.gemm_ctas = gemm_ctas
         self.chunks = row_chunks(S, self.o_chunks)
         self.comm_stream = torch.cuda.Stream(self.device) if self.o_chunks > 1 else None
-        if reduce not in ("all_reduce", "rs_ag"):
-            raise ValueError("reduce must be 'all_reduce' or 'rs_ag'")
+        if reduce not in ("all_reduce", "rs_ag", "p2p"):
+            raise ValueError("reduce must be 'all_reduce', 'rs_ag' or 'p2p'")
         self.reduce = reduce if (world > 1 and (B * S) % world == 0) else "all_reduce"
+        self.peer = None
+        if self.reduce == "p2p":
+            if B != 1:
+                raise ValueError("reduce='p2p' takes one sequence")
+            self.peer = PeerExchange(S, hidden, rank, world, group, self.device)
+            self.partial, self.out = self.peer.partial.view(B, S, hidden), self.peer.out.view(B, S, hidden)
         self._mine = (mk(B * S // world, hidden, dt=torch.float32) if self.reduce == "rs_ag" else None)
         self._mine_bf = (mk(B * S // world, hidden) if self.reduce == "rs_ag" else None)
 
@@ -183,6 +282,10 @@ class FullLayerSession:
         if self.world == 1:
             self._core()
             return kernels.o_proj(self.attn, self.wo, out=self.out)
+        if self.reduce == "p2p":
+            self.run_partial()
+            self.peer.reduce_gather()
+            return self.out
         if self.reduce == "rs_ag":
             self.run_partial()
             return reduce_cast_gather(self.partial, self.out, self.world, self.group, mine=self._mine,
@@ -201,6 +304,12 @@ class FullLayerSession:
 
         pipelined_row_reduce(part, self.chunks, compute, self.world, self.group, finish, self.comm_stream)
         return self.out
+
+    def close(self) -> None:
+        """Release the peer-memory exchange (collective when reduce='p2p')."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def run_host(self, h_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
         """h_host [B,S,hidden] / out_host [B,S,hidden]: bf16 CPU tensors (pinned for async copies)."""
