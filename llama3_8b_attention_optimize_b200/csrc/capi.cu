@@ -100,8 +100,8 @@ extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   }
   if (first == 0) return GQA_OK;
   if (site) *site = first;
-  // sites 0x300-0x3ff are checks of device-side input data, the rest are bounded waits
-  return (first >= 0x300 && first < 0x400) ? GQA_ERR_DEVICE_INPUT : GQA_ERR_DEVICE_TIMEOUT;
+  // sites 0x600-0x6ff are checks of device-side input data, the rest are bounded waits
+  return (first >= 0x600 && first < 0x700) ? GQA_ERR_DEVICE_INPUT : GQA_ERR_DEVICE_TIMEOUT;
 }
 
 extern "C" int gqa_prefill_bf16(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin,

@@ -63,7 +63,7 @@ enum : int {
   SITE_SOFTMAX = 0x203,
   SITE_DRAIN = 0x204,
   SITE_SMEM_ALIGN = 0x205,
-  SITE_BAD_PAGE = 0x301,  // a block-table entry outside [0, num_pages) (input error)
+  SITE_BAD_PAGE = 0x601,  // a block-table entry outside [0, num_pages) (input error)
 };
 
 struct Params {

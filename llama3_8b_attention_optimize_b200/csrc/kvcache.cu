@@ -27,8 +27,8 @@ constexpr int kD = 128;
 constexpr int kWarps = 8;
 
 enum : int {
-  SITE_CAPACITY = 0x302,  // lens[b] + i beyond the cache
-  SITE_BAD_PAGE = 0x303,  // block-table entry outside [0, num_pages)
+  SITE_CAPACITY = 0x602,  // lens[b] + i beyond the cache
+  SITE_BAD_PAGE = 0x603,  // block-table entry outside [0, num_pages)
 };
 
 struct Params {
