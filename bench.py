@@ -437,7 +437,7 @@ def run_layer(args, world, rank, dev, stream) -> dict:
         ls.run_device()
         ref = ls.out.clone()
         variants = []
-        for mode, chunks, ctas in (("p2p", 1, 0), ("rs_ag", 1, 0), ("all_reduce", 4, 132)):
+        for mode, chunks, ctas in (("p2p_fused", 1, 0), ("p2p", 1, 0), ("rs_ag", 1, 0), ("all_reduce", 4, 132)):
             try:  # raised on every rank together when peer mapping is unavailable
                 lc = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev, o_chunks=chunks, gemm_ctas=ctas,
                                       reduce=mode)

@@ -173,6 +173,15 @@ int gqa_peer_close(void* peer_ptr);
 int gqa_peer_free(void* dev_ptr);
 int gqa_tp_reduce_gather_bf16(const void* const* bases, int world, int rank, int S, int N, unsigned int epoch,
                               gqa_stream_t stream);
+/* The same exchange fused into the o_proj (one sequence): the GEMM of attn [Hq][S][128]
+ * against wo (ldw, the shard's columns) stores each fp32 row straight into the owning
+ * rank's buffer (NVLink peer stores while other tiles still compute) and signals the
+ * owners when its grid is done; each owner sums its block, rounds once and stores the
+ * bf16 block into every rank's out.  The buffer's out holds the full result when the
+ * stream reaches that point.  (S / world) % 128 == 0, N % 256 == 0.                   */
+int gqa_tp_o_proj_exchange_bf16(const void* attn, const void* wo, int ldw, const void* const* bases, int world,
+                                int rank, int S, int Hq, int head_dim, int N, unsigned int epoch,
+                                gqa_stream_t stream);
 
 /* ---------------------------------------------------------------- paged K/V cache
  * The step after decode (the reference has no serving cache): append each step's new

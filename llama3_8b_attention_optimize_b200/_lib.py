@@ -63,6 +63,8 @@ SIGNATURES = {
     "gqa_peer_close": (_i, [_vp]),
     "gqa_peer_free": (_i, [_vp]),
     "gqa_tp_reduce_gather_bf16": (_i, [ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, ctypes.c_uint, _vp]),
+    "gqa_tp_o_proj_exchange_bf16": (_i, [_vp, _vp, _i, ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, _i, _i,
+                                         ctypes.c_uint, _vp]),
     "gqa_o_proj_rows_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
 }
 

@@ -38,6 +38,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
 constexpr int kMaxRegions = 3;
+constexpr int kMaxDest = 8;
 
 template <int BN>
 struct Cfg {
@@ -79,6 +80,14 @@ struct Params {
   const uint16_t* cos;  // [pos0 + S][128] bf16 (rope regions only)
   const uint16_t* sin;
   int pos0;
+  // Scatter epilogue (scatter_rows > 0, fp32 only): row m goes to dst[m / scatter_rows] +
+  // (m % scatter_rows) * N by direct stores (dst may be NVLink peer memory); when the grid
+  // is done, the last CTA raises sig_flag[q] = sig_epoch at every destination q.
+  int scatter_rows, n_dest;
+  float* dst[kMaxDest];
+  uint32_t* sig_flag[kMaxDest];
+  uint32_t* sig_counter;  // zero between launches
+  uint32_t sig_epoch;
 };
 
 struct Maps {
@@ -97,6 +106,31 @@ __device__ __forceinline__ int region_of(const Params& p, int n0) {
 // Region r without a dynamically indexed parameter array (which would go to local memory).
 __device__ __forceinline__ Region region_at(const Params& p, int r) {
   return r == 0 ? p.reg[0] : (r == 1 ? p.reg[1] : p.reg[2]);
+}
+
+__device__ __forceinline__ float* dst_at(const Params& p, int q) {
+  switch (q) {
+    case 0: return p.dst[0];
+    case 1: return p.dst[1];
+    case 2: return p.dst[2];
+    case 3: return p.dst[3];
+    case 4: return p.dst[4];
+    case 5: return p.dst[5];
+    case 6: return p.dst[6];
+    default: return p.dst[7];
+  }
+}
+__device__ __forceinline__ uint32_t* flag_at(const Params& p, int q) {
+  switch (q) {
+    case 0: return p.sig_flag[0];
+    case 1: return p.sig_flag[1];
+    case 2: return p.sig_flag[2];
+    case 3: return p.sig_flag[3];
+    case 4: return p.sig_flag[4];
+    case 5: return p.sig_flag[5];
+    case 6: return p.sig_flag[6];
+    default: return p.sig_flag[7];
+  }
 }
 
 __device__ __forceinline__ const CUtensorMap* pick(const CUtensorMap* m0, const CUtensorMap* m1,
@@ -314,7 +348,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
-        if (et == 0 && ok) {
+        if (p.scatter_rows > 0) {
+          // rows go to their owner (possibly NVLink peer memory) by plain stores, 8
+          // consecutive threads per 128-byte row segment so every line is written whole
+          const int q = m0 / p.scatter_rows;  // a tile never straddles two owners
+          float* dbase = dst_at(p, q) + static_cast<size_t>(m0 - q * p.scatter_rows) * p.N + n0 + cyc * 64;
+#pragma unroll 4
+          for (int idx = et; idx < 2 * 128 * 8; idx += 128) {
+            const int box = idx >> 10, rr = (idx >> 3) & 127, j = idx & 7;
+            const uint4 v = *reinterpret_cast<const uint4*>((box ? stg1_p : stg0_p) + box_unit(rr, j));
+            if (ok && m0 + rr < p.M)
+              *reinterpret_cast<uint4*>(dbase + static_cast<size_t>(rr) * p.N + box * 32 + 4 * j) = v;
+          }
+          named_bar_sync(1, 128);  // staging free again (the next cycle refills it)
+        } else if (et == 0 && ok) {
           if (p.out_f32) {
             const int nc = n0 - rg.n0 + cyc * 64;
             tma_store_4d(cm, stg0, nc, m0, 0, 0);
@@ -333,11 +380,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       }
     }
     if (et == 0) bulk_wait0();
+    if (p.scatter_rows > 0) __threadfence_system();  // this thread's direct stores, before the signal
   }
 
   // ---- teardown
   tc_fence_before();
   __syncthreads();
+  if (p.scatter_rows > 0 && threadIdx.x == 0) {
+    // the last CTA to finish tells every destination that its rows are complete
+    if (atomicAdd(p.sig_counter, 1u) + 1u == gridDim.x) {
+      *p.sig_counter = 0u;
+      __threadfence_system();
+      for (int q = 0; q < p.n_dest; ++q)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag_at(p, q)), "r"(p.sig_epoch) : "memory");
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
@@ -364,6 +421,11 @@ struct Launch {
   const void* sin;
   int pos0;
   int max_ctas;  // persistent grid cap (0 = one CTA per SM), e.g. to leave SMs to a collective
+  int scatter_rows, n_dest;  // scatter epilogue (see Params)
+  float* dst[kMaxDest];
+  uint32_t* sig_flag[kMaxDest];
+  uint32_t* sig_counter;
+  uint32_t sig_epoch;
 };
 
 template <int BN>
@@ -402,6 +464,14 @@ int launch_bn(const Launch& L, cudaStream_t stream) {
   p.cos = static_cast<const uint16_t*>(L.cos);
   p.sin = static_cast<const uint16_t*>(L.sin);
   p.pos0 = L.pos0;
+  p.scatter_rows = L.scatter_rows;
+  p.n_dest = L.n_dest;
+  for (int q = 0; q < kMaxDest; ++q) {
+    p.dst[q] = L.dst[q];
+    p.sig_flag[q] = L.sig_flag[q];
+  }
+  p.sig_counter = L.sig_counter;
+  p.sig_epoch = L.sig_epoch;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -641,6 +711,57 @@ extern "C" int gqa_o_proj_rows_bf16(const void* attn, const void* wo, void* out,
   L.max_ctas = max_ctas;
   return gemm::launch(L, static_cast<cudaStream_t>(stream));
 }
+
+namespace gqa {
+// o_proj (B = 1) whose fp32 rows go straight to their owners: row m to dst[m / (S / world)]
+// + (m % (S / world)) * N, then the grid's last CTA raises flags[q] = epoch for every q.
+int launch_o_proj_scatter(const void* attn, const void* wo, int S, int Hq, int N, int ldw, float* const* dst,
+                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, cudaStream_t stream) {
+  if (!attn || !wo || !dst || !flags || !counter || world < 1 || world > gemm::kMaxDest) return GQA_ERR_INVALID_ARGUMENT;
+  if (S <= 0 || Hq <= 0 || N <= 0 || S % world || (S / world) % gemm::kBM || N % 256) return GQA_ERR_UNSUPPORTED;
+  if (ldw < Hq * 128 || ldw % 8) return GQA_ERR_INVALID_ARGUMENT;
+  if (bad16(attn) || bad16(wo)) return GQA_ERR_MISALIGNED;
+  for (int q = 0; q < world; ++q)
+    if (!dst[q] || bad16(dst[q]) || !flags[q]) return GQA_ERR_INVALID_ARGUMENT;
+  gemm::Launch L{};
+  L.a = attn;
+  L.a_dims[0] = 128;
+  L.a_dims[1] = S;
+  L.a_dims[2] = Hq;
+  L.a_dims[3] = 1;
+  L.a_strides[0] = 256;
+  L.a_strides[1] = 256LL * S;
+  L.a_strides[2] = 256LL * S * Hq;
+  L.a_kin = 128;
+  L.M = S;
+  L.N = N;
+  L.K = Hq * 128;
+  L.S = S;
+  L.out_f32 = 1;
+  L.n_regions = 1;
+  L.reg[0] = gemm::Region{0, N, 0, 0};
+  L.w[0] = wo;
+  L.ldw[0] = ldw;
+  // the staging / TMA-store map is built but unused in scatter mode: any valid fp32 view
+  L.c[0] = dst[0];
+  L.c_dims[0][0] = N;
+  L.c_dims[0][1] = S / world;
+  L.c_dims[0][2] = 1;
+  L.c_dims[0][3] = 1;
+  L.c_strides[0][0] = static_cast<long long>(N) * 4;
+  L.c_strides[0][1] = L.c_strides[0][0] * (S / world);
+  L.c_strides[0][2] = L.c_strides[0][1];
+  L.scatter_rows = S / world;
+  L.n_dest = world;
+  for (int q = 0; q < gemm::kMaxDest; ++q) {
+    L.dst[q] = dst[q < world ? q : 0];
+    L.sig_flag[q] = flags[q < world ? q : 0];
+  }
+  L.sig_counter = counter;
+  L.sig_epoch = epoch;
+  return gemm::launch(L, stream);
+}
+}  // namespace gqa
 
 namespace {
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ src, uint16_t* __restrict__ dst, long long n) {

@@ -59,6 +59,9 @@ int launch_prefill8(const void* q, const void* k, const void* v, void* o, const 
                     int S, int Hq, int Hkv, int kv_begin, int kv_count, float scale, int flags, cudaStream_t stream,
                     long long* trace = nullptr, int trace_block = -1);
 
+int launch_o_proj_scatter(const void* attn, const void* wo, int S, int Hq, int N, int ldw, float* const* dst,
+                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, cudaStream_t stream);
+
 int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
                      const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,
                      int kv_begin, int kv_count, int split_len, int n_splits, float scale, int flags,

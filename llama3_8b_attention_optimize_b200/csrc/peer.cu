@@ -182,6 +182,86 @@ __global__ void __launch_bounds__(kThreads) tp_gather_kernel(const Params prm) {
   }
 }
 
+// ---------------------------------------------------------------- push variant
+// The o_proj GEMM itself stores each row of its fp32 partial into the owner's buffer:
+// rank r's rows of owner q's block land in q's slot r (the buffer's fp32 region read as
+// [world][S / world][N]); its last CTA raises flagA[r] = e at every owner.  Then:
+//   tp_reduce_push: wait until flagA[0..world) of the local buffer are e, sum the local
+//     slots in rank order, round once, store the bf16 block into every rank's out (P2P
+//     stores), and the last block raises flagB[rank] = e at every rank;
+//   tp_wait: wait until flagB[0..world) of the local buffer are e.
+// All peer traffic is stores, issued while the GEMM is still computing other tiles.
+struct PushParams {
+  uint16_t* out[kMaxRanks];         // each rank's bf16 out [S][N]
+  uint32_t* flag_b[kMaxRanks];      // flagB[rank] in each rank's buffer
+  const float* slots;               // local [world][S / world][N]
+  const uint32_t* local_a;          // local flagA[world]
+  const uint32_t* local_b;          // local flagB[world]
+  uint32_t* counter;                // local block counter
+  int world, rank, S, N;
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ uint16_t* out_at(const PushParams& p, int q) {
+  switch (q) {
+    case 0: return p.out[0];
+    case 1: return p.out[1];
+    case 2: return p.out[2];
+    case 3: return p.out[3];
+    case 4: return p.out[4];
+    case 5: return p.out[5];
+    case 6: return p.out[6];
+    default: return p.out[7];
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) tp_reduce_push_kernel(const PushParams prm) {
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int r = 0; r < prm.world && ok; ++r) ok = wait_flag(prm.local_a + r, prm.epoch, SITE_READY);
+    ok_s = ok ? 1 : 0;
+  }
+  __syncthreads();
+  const int rows = prm.S / prm.world;
+  const long long n4 = static_cast<long long>(rows) * prm.N / 4;
+  const long long out_base = static_cast<long long>(prm.rank) * rows * prm.N;  // elements
+  if (ok_s) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
+      // slots were written by other GPUs: read past L1
+      float4 acc = __ldcg(reinterpret_cast<const float4*>(prm.slots) + i);
+      for (int r = 1; r < prm.world; ++r) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(prm.slots + static_cast<size_t>(r) * rows * prm.N) + i);
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+      uint2 w;
+      w.x = static_cast<uint32_t>(f2bf_bits(acc.x)) | (static_cast<uint32_t>(f2bf_bits(acc.y)) << 16);
+      w.y = static_cast<uint32_t>(f2bf_bits(acc.z)) | (static_cast<uint32_t>(f2bf_bits(acc.w)) << 16);
+      for (int q = 0; q < prm.world; ++q) reinterpret_cast<uint2*>(out_at(prm, q) + out_base)[i] = w;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(prm.counter, 1u) + 1u == gridDim.x) {
+      *prm.counter = 0u;
+      __threadfence_system();
+      if (ok_s)
+        for (int q = 0; q < prm.world; ++q) st_release_sys(prm.flag_b[q], prm.epoch);
+    }
+  }
+}
+
+__global__ void tp_wait_kernel(const PushParams prm) {
+  if (threadIdx.x == 0)
+    for (int q = 0; q < prm.world; ++q)
+      if (!wait_flag(prm.local_b + q, prm.epoch, SITE_DONE)) break;
+}
+
 }  // namespace peer
 
 GQA_ERROR_FLAG_ACCESSOR(error_flag_peer)
@@ -263,8 +343,58 @@ extern "C" int gqa_tp_reduce_gather_bf16(const void* const* bases, int world, in
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 
-// [partial fp32 S x N][out bf16 S x N][ready u32][done u32][block counter u32] (+ pad)
+// [partial fp32 S x N][out bf16 S x N][flags 256 B]; flags: pull variant ready @0,
+// done @4, counter @8; push variant flagA[8] @64, flagB[8] @96, reduce counter @128,
+// GEMM counter @132.
 extern "C" size_t gqa_tp_buffer_bytes(int S, int N) {
   if (S <= 0 || N <= 0) return 0;
   return static_cast<size_t>(S) * N * 6 + 256;
+}
+
+extern "C" int gqa_tp_o_proj_exchange_bf16(const void* attn, const void* wo, int ldw, const void* const* bases,
+                                           int world, int rank, int S, int Hq, int head_dim, int N,
+                                           unsigned int epoch, gqa_stream_t stream) {
+  using namespace gqa;
+  using namespace gqa::peer;
+  if (!attn || !wo || !bases || world < 2 || world > kMaxRanks || rank < 0 || rank >= world)
+    return GQA_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return GQA_ERR_UNSUPPORTED;
+  if (S <= 0 || N <= 0 || Hq <= 0 || epoch == 0) return GQA_ERR_INVALID_ARGUMENT;
+  if (S % world || (S / world) % 128 || N % 256) return GQA_ERR_UNSUPPORTED;
+  const size_t slot_bytes = static_cast<size_t>(S / world) * N * 4;
+  const size_t part_bytes = static_cast<size_t>(S) * N * 4, out_bytes = static_cast<size_t>(S) * N * 2;
+  float* dst[kMaxRanks];
+  uint32_t* flag_a[kMaxRanks];
+  PushParams pp{};
+  for (int q = 0; q < world; ++q) {
+    uint8_t* b = static_cast<uint8_t*>(const_cast<void*>(bases[q]));
+    if (!b || (reinterpret_cast<uintptr_t>(b) & 255u)) return GQA_ERR_MISALIGNED;
+    uint8_t* flags = b + part_bytes + out_bytes;
+    dst[q] = reinterpret_cast<float*>(b + static_cast<size_t>(rank) * slot_bytes);  // my slot at owner q
+    flag_a[q] = reinterpret_cast<uint32_t*>(flags + 64) + rank;
+    pp.out[q] = reinterpret_cast<uint16_t*>(b + part_bytes);
+    pp.flag_b[q] = reinterpret_cast<uint32_t*>(flags + 96) + rank;
+  }
+  uint8_t* mine = static_cast<uint8_t*>(const_cast<void*>(bases[rank]));
+  uint8_t* mflags = mine + part_bytes + out_bytes;
+  pp.slots = reinterpret_cast<const float*>(mine);
+  pp.local_a = reinterpret_cast<const uint32_t*>(mflags + 64);
+  pp.local_b = reinterpret_cast<const uint32_t*>(mflags + 96);
+  pp.counter = reinterpret_cast<uint32_t*>(mflags + 128);
+  pp.world = world;
+  pp.rank = rank;
+  pp.S = S;
+  pp.N = N;
+  pp.epoch = epoch;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = launch_o_proj_scatter(attn, wo, S, Hq, N, ldw, dst, flag_a, world, reinterpret_cast<uint32_t*>(mflags + 132),
+                                 epoch, st);
+  if (rc != GQA_OK) return rc;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  tp_reduce_push_kernel<<<2 * sms, kThreads, 0, st>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
+  tp_wait_kernel<<<1, 32, 0, st>>>(pp);
+  return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }

@@ -16,6 +16,11 @@ step): the o_proj partial goes straight into a CUDA-IPC buffer every rank maps
 (``PeerExchange``), each rank sums its row block of all partials by P2P loads, rounds
 once and gathers the other blocks (``gqa_tp_reduce_gather_bf16``).
 
+``reduce="p2p_fused"`` goes one step further: the o_proj GEMM's epilogue stores each fp32
+row straight into the owning rank's buffer (NVLink stores while other tiles compute), and
+the owners reduce, round and store their bf16 blocks into every rank's output
+(``gqa_tp_o_proj_exchange_bf16``).
+
 ``reduce="rs_ag"`` replaces 4-5 by a reduce-scatter of the fp32 partials (each rank sums
 S/world rows), the rounding of those rows, and an all-gather of the bf16 rows: the same
 one rounding of the fp32 sum, with 3/4 of the all-reduce's bytes on the links.
@@ -171,6 +176,18 @@ class PeerExchange:
                       "gqa_tp_reduce_gather_bf16")
         return self.out
 
+    def o_proj_exchange(self, attn: torch.Tensor, wo: torch.Tensor) -> torch.Tensor:
+        """The o_proj of attn [Hq, S, 128] (this rank's heads) against wo [N, Hq*128]
+        fused with the exchange: rows go straight to their owners over NVLink; returns
+        the full bf16 result in ``out``."""
+        self.epoch += 1
+        Hq = attn.shape[-3]
+        kernels.check(self.lib.gqa_tp_o_proj_exchange_bf16(kernels._ptr(attn), kernels._ptr(wo), wo.shape[1],
+                                                           self._bases, self.world, self.rank, self.S, Hq, 128,
+                                                           self.N, self.epoch, kernels._stream(self.device)),
+                      "gqa_tp_o_proj_exchange_bf16")
+        return self.out
+
     def close(self) -> None:
         import torch.distributed as dist
 
@@ -241,11 +258,11 @@ class FullLayerSession:
         self.gemm_ctas = gemm_ctas
         self.chunks = row_chunks(S, self.o_chunks)
         self.comm_stream = torch.cuda.Stream(self.device) if self.o_chunks > 1 else None
-        if reduce not in ("all_reduce", "rs_ag", "p2p"):
-            raise ValueError("reduce must be 'all_reduce', 'rs_ag' or 'p2p'")
+        if reduce not in ("all_reduce", "rs_ag", "p2p", "p2p_fused"):
+            raise ValueError("reduce must be 'all_reduce', 'rs_ag', 'p2p' or 'p2p_fused'")
         self.reduce = reduce if (world > 1 and (B * S) % world == 0) else "all_reduce"
         self.peer = None
-        if self.reduce == "p2p":
+        if self.reduce in ("p2p", "p2p_fused"):
             if B != 1:
                 raise ValueError("reduce='p2p' takes one sequence")
             self.peer = PeerExchange(S, hidden, rank, world, group, self.device)
@@ -285,6 +302,10 @@ class FullLayerSession:
         if self.reduce == "p2p":
             self.run_partial()
             self.peer.reduce_gather()
+            return self.out
+        if self.reduce == "p2p_fused":
+            self._core()
+            self.peer.o_proj_exchange(self.attn[0], self.wo)
             return self.out
         if self.reduce == "rs_ag":
             self.run_partial()

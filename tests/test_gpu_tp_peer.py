@@ -43,17 +43,21 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
         wo = (torch.randn(4096, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
         ref = FullLayerSession(S, rank=rank, world=world, device=dev)
         p2p = FullLayerSession(S, rank=rank, world=world, device=dev, reduce="p2p")
-        ref.set_weights(wq, wk, wv, wo)
-        p2p.set_weights(wq, wk, wv, wo)
+        fused = FullLayerSession(S, rank=rank, world=world, device=dev, reduce="p2p_fused")
+        for sess in (ref, p2p, fused):
+            sess.set_weights(wq, wk, wv, wo)
         for step in range(4):  # new input every step: no stale blocks survive an epoch
             h = torch.randn(ref.h.shape, generator=g, device=dev).to(torch.bfloat16)
-            ref.h.copy_(h)
-            p2p.h.copy_(h)
+            for sess in (ref, p2p, fused):
+                sess.h.copy_(h)
             a = ref.run_device().clone()
             b = p2p.run_device().clone()
+            c = fused.run_device().clone()
             K.device_check(dev)
             assert torch.equal(a, b), (rank, step, (a.float() - b.float()).abs().max().item())
+            assert torch.equal(a, c), (rank, step, (a.float() - c.float()).abs().max().item())
         p2p.close()
+        fused.close()
         with open(os.path.join(out_dir, f"rank{rank}.ok"), "w") as f:
             f.write("ok")
     finally:
