@@ -468,7 +468,9 @@ def run_layer(args, world, rank, dev, stream) -> dict:
 
 def run_profile_case(args):
     """Small cases for ncu captures (inputs > L2, a few hundred MB on the device):
-    prefill: B=2, seq 8192, 32/8 heads, fused RoPE; decode: B=8, cache 32768 keys."""
+    prefill: B=2, seq 8192, 32/8 heads, fused RoPE; decode: B=8, cache 32768 keys;
+    decode_paged: the same decode over shuffled 128-key pages, plus one RoPE-on-append of a
+    token per sequence."""
     from llama3_8b_attention_optimize_b200 import kernels
     from llama3_8b_attention_optimize_b200.session import DecodeSession, PrefillSession
     torch.cuda.set_device(0)
@@ -486,9 +488,26 @@ def run_profile_case(args):
         kc = torch.randn(B, HKV, DEC_LMAX, D, generator=gen, device=dev).to(torch.bfloat16)
         vc = torch.randn(B, HKV, DEC_LMAX, D, generator=gen, device=dev).to(torch.bfloat16)
         ds.q.copy_(torch.randn(ds.q.shape, generator=gen, device=dev))
-        ds.lens.copy_(torch.randint(1024, DEC_LMAX + 1, (B,), generator=torch.Generator().manual_seed(99),
-                                    dtype=torch.int32).to(dev))
+        lens = torch.randint(1024, DEC_LMAX + 1, (B,), generator=torch.Generator().manual_seed(99), dtype=torch.int32)
+        ds.lens.copy_(lens.to(dev))
         fn = lambda: ds.run_device(kc, vc)  # noqa: E731
+        if args.profile_case == "decode_paged":
+            P, n_lp = 128, DEC_LMAX // 128
+            perm = torch.randperm(B * n_lp, generator=torch.Generator().manual_seed(7)).to(torch.int32)
+            table = perm.view(B, n_lp).to(dev)
+            kp = kc.view(B, HKV, n_lp, P, D).transpose(1, 2).reshape(B * n_lp, HKV, P, D)
+            vp = vc.view(B, HKV, n_lp, P, D).transpose(1, 2).reshape(B * n_lp, HKV, P, D)
+            kpool, vpool = torch.empty_like(kp), torch.empty_like(vp)
+            kpool[perm.to(dev, torch.long)] = kp
+            vpool[perm.to(dev, torch.long)] = vp
+            del kp, vp, kc, vc
+            kn = torch.randn(B, HKV, 1, D, generator=gen, device=dev).to(torch.bfloat16)
+            short = (ds.lens - 1).clamp(min=0)  # append into the last cached row: stays in the pool
+
+            def fn():
+                kernels.kv_append(kn, kn, kpool, vpool, short, cos=ds.cos, sin=ds.sin, block_table=table)
+                kernels.decode_paged(ds.q, kpool, vpool, table, ds.lens, q_pos=ds.lens, cos=ds.cos, sin=ds.sin,
+                                     workspace=ds.ws, out=ds.o)
     for _ in range(args.warmup + args.steps):
         fn()
     kernels.device_check(dev)
@@ -498,7 +517,7 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "decode_paged"], default=None,
                     help="run a small case for ncu captures instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
