@@ -399,6 +399,12 @@ def run_decode_paged(args, world, dev, stream, ds, kc, vc, lens_all, hkv, dec_by
             "gpu_launches": 2 * dsteps + dsteps}
 
 
+# Largest rank counts the NVLink peer-memory o_proj exchanges have been run and checked
+# against the NCCL path on (tests/test_gpu_tp_peer.py and this bench's variant check).
+P2P_FUSED_CHECKED_RANKS = 2
+P2P_CHECKED_RANKS = 4
+
+
 def run_layer(args, world, rank, dev, stream) -> dict:
     from llama3_8b_attention_optimize_b200 import kernels
     from llama3_8b_attention_optimize_b200.layer import FullLayerSession, reduce_partials
@@ -437,7 +443,12 @@ def run_layer(args, world, rank, dev, stream) -> dict:
         ls.run_device()
         ref = ls.out.clone()
         variants = []
+        # peer-memory exchanges run only at rank counts they have been checked on
+        checked_up_to = {"p2p_fused": P2P_FUSED_CHECKED_RANKS, "p2p": P2P_CHECKED_RANKS}
         for mode, chunks, ctas in (("p2p_fused", 1, 0), ("p2p", 1, 0), ("rs_ag", 1, 0), ("all_reduce", 4, 132)):
+            if world > checked_up_to.get(mode, world):
+                variants.append({"reduce": mode, "skipped": f"checked on up to {checked_up_to[mode]} GPUs"})
+                continue
             try:  # raised on every rank together when peer mapping is unavailable
                 lc = FullLayerSession(LAYER_S, rank=rank, world=world, device=dev, o_chunks=chunks, gemm_ctas=ctas,
                                       reduce=mode)
