@@ -481,13 +481,18 @@ def run_profile_case(args):
     """Small cases for ncu captures (inputs > L2, a few hundred MB on the device):
     prefill: B=2, seq 8192, 32/8 heads, fused RoPE; decode: B=8, cache 32768 keys;
     decode_paged: the same decode over shuffled 128-key pages, plus one RoPE-on-append of a
-    token per sequence."""
+    token per sequence; gemm: the projection GEMM at 4096 x 4096 x 4096 (bf16 out)."""
     from llama3_8b_attention_optimize_b200 import kernels
     from llama3_8b_attention_optimize_b200.session import DecodeSession, PrefillSession
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(7)
-    if args.profile_case == "prefill":
+    if args.profile_case == "gemm":
+        x = (torch.randn(4096, 4096, generator=gen, device=dev)).to(torch.bfloat16)
+        w = (torch.randn(4096, 4096, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(4096, 4096, dtype=torch.bfloat16, device=dev)
+        fn = lambda: kernels.linear(x, w, out=y)  # noqa: E731
+    elif args.profile_case == "prefill":
         sess = PrefillSession(2, S_PREFILL, HQ, HKV, D, rope=args.rope, device=dev)
         sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev) * 2.5)
         sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev) * 2.5)
@@ -528,7 +533,7 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "decode_paged"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "decode_paged", "gemm"], default=None,
                     help="run a small case for ncu captures instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
