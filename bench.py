@@ -185,6 +185,62 @@ def cpu_reference_sample(heads: int, S: int, seed: int = 7):
     return dt, causal_flops(1, heads, S, D), os.cpu_count()
 
 
+# The reference's one published figure: CPU_Baseline fp32 at 32 q heads, 8 kv heads,
+# seq 128, head_dim 128, median of 50 runs after 10 warm-up runs, on its author's CPU.
+REFERENCE_C1_PUBLISHED_MS = 2.088770
+
+
+def cpu_small_configs() -> dict:
+    """The NumPy port of gqa_attention_cpu at the reference's own benchmark settings:
+    seq 128 (its published configuration; warm-up 10, repeat 50, median, as its
+    run_benchmark times it) and seq 2048 (warm-up 1, repeat 3), fp32, generate_qkv inputs."""
+    from oracle import cpu_port
+
+    out = {"c1_published_ms": REFERENCE_C1_PUBLISHED_MS,
+           "small_configs": "CPU_Baseline llama3_like shapes (32 q / 8 kv heads, d 128), fp32, causal, "
+                            "generate_qkv(seed 2026), all host threads"}
+    for key, S, warm, rep in (("c1", 128, 10, 50), ("c2", 2048, 1, 3)):
+        cfg = cpu_port.BaselineConfig(q_heads=HQ, kv_heads=HKV, seq_len=S, head_dim=D)
+        q, k, v = cpu_port.generate_qkv(cfg)
+        for _ in range(warm):
+            cpu_port.gqa_attention_cpu(q, k, v, cfg)
+        ts = []
+        for _ in range(rep):
+            t0 = time.perf_counter()
+            cpu_port.gqa_attention_cpu(q, k, v, cfg)
+            ts.append(time.perf_counter() - t0)
+        out[f"{key}_ms"] = 1e3 * statistics.median(ts)
+        out[f"{key}_repeat"] = rep
+    return out
+
+
+def run_short_prefills(args, hq, hkv, dev, stream, world) -> dict:
+    """Batch 1 prefill at seq 128 and seq 2048 (this rank's heads), timed like the
+    headline step; at these sizes launch overhead and wave quantisation dominate."""
+    from llama3_8b_attention_optimize_b200 import kernels
+    from llama3_8b_attention_optimize_b200.session import PrefillSession
+
+    out = {}
+    gen = torch.Generator(device=dev).manual_seed(2026)
+    for key, S in (("c1", 128), ("c2", 2048)):
+        sess = PrefillSession(1, S, hq, hkv, D, causal=True, rope=args.rope, device=dev)
+        sess.q.copy_(torch.randn(sess.shape_q, generator=gen, device=dev))
+        sess.k.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
+        sess.v.copy_(torch.randn(sess.shape_kv, generator=gen, device=dev))
+        for _ in range(max(args.warmup, 10)):
+            sess.run_device()
+        kernels.device_check(dev)
+        n = 200
+        ms = time_loop(sess.run_device, n, world, stream) / n
+        kernels.device_check(dev)
+        fl = causal_flops(1, HQ, S, D)  # every rank runs its heads of the one sequence
+        out[key] = {"seq_len": S, "batch": 1, "ms_per_step": ms, "value": fl / (ms * 1e-3) / 1e12,
+                    "unit": "TFLOP/s", "steps": n, "launches_per_step": sess.launches_per_step(),
+                    "l2": "inputs fit in L2 (no flush between steps)"}
+        del sess
+    return out
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
@@ -243,6 +299,23 @@ def run_ours(args, world, rank, local):
     ms_step = ms / args.steps
     flops_total = causal_flops(B, HQ, S_PREFILL, D)
     value = flops_total / (ms_step * 1e-3) / 1e12
+
+    # ---- the same step back to back for >= 2 s: the clock the power cap settles at
+    sustained = None
+    if args.sustained_s > 0:
+        n_sus = max(args.steps, int(args.sustained_s * 1e3 / ms_step) + 1)
+        with ClockSampler(local) as clk_s:
+            t_a = time.monotonic()
+            ms_sus = time_loop(sess.run_device, n_sus, world, stream)
+            clk_s.window(t_a, time.monotonic())
+        kernels.device_check(dev)
+        sustained = {"value": flops_total / (ms_sus / n_sus * 1e-3) / 1e12, "unit": "TFLOP/s",
+                     "ms_per_step": ms_sus / n_sus, "steps": n_sus, "timed_s": ms_sus * 1e-3,
+                     "clocks": clk_s.summary()}
+
+    # ---- the smaller prefill configurations (one sequence, one GPU's share of heads):
+    # S=128 (the reference's CPU-runnable core) and S=2048, same mode as the headline
+    short = run_short_prefills(args, hq, hkv, dev, stream, world)
 
     # ---- end to end through the host-buffer API (pinned host in, pinned host out); every
     # step copies its Q/K/V in and its O out, overlapped across steps on three streams
@@ -308,6 +381,10 @@ def run_ours(args, world, rank, local):
         cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                "sample": "24 query heads (kv head 0, batch element 0) of the seq-8192 workload, NumPy fp32 "
                          "(CPU_Baseline gqa_attention_cpu restated), %.1f s" % dt}
+        cpu.update(cpu_small_configs())
+        for key, gpu in (("c1", short["c1"]), ("c2", short["c2"])):
+            cpu[f"{key}_gpu_ms"] = gpu["ms_per_step"]
+            cpu[f"{key}_speedup"] = cpu[f"{key}_ms"] / gpu["ms_per_step"]
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -328,7 +405,12 @@ def run_ours(args, world, rank, local):
                               "kv_heads_per_gpu": hkv}, "roofline": dec_roof, "gpu_launches": 2 * dsteps},
         "decode_paged": paged,
         "full_layer": layer,
+        "short_prefill": short,
     }
+    if sustained is not None:
+        sustained["frac_of_sustained_peak"] = (sustained["value"] / world) / tc_sust if tc_sust else None
+        sustained["frac_of_burst_peak"] = (sustained["value"] / world) / tc_peak
+        line["sustained"] = sustained
     lt = layer["achieved_per_gpu"]
     layer["roofline"] = {"bound": "tensor", "achieved": lt, "peak": tc_peak, "unit": "TFLOP/s", "frac": lt / tc_peak}
     if cpu is not None:
@@ -545,6 +627,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sustained-s", type=float, default=2.0,
+                    help="also time the headline step back to back for this many seconds (0: skip)")
     ap.add_argument("--rope", choices=["prepass_k", "fused", "none"], default="prepass_k",
                     help="prepass_k: K rotated once by its own kernel, Q rotated inside the fused kernel; "
                          "fused: both rotated inside the fused kernel")

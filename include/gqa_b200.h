@@ -12,7 +12,10 @@
  *
  * Conventions for every entry point:
  *  - All tensors are caller-owned DEVICE buffers of raw bf16 words (uint16),
- *    contiguous, 16-byte aligned.  The library never allocates device memory.
+ *    contiguous, 16-byte aligned.  The compute entry points allocate no device
+ *    memory.  Two exceptions: gqa_peer_alloc (the one call that allocates: an
+ *    exchange buffer for the tensor-parallel o_proj) and a fixed 16 MiB scratch
+ *    array per GPU compiled into the library for gqa_decode_bf16_noalloc.
  *  - Layouts follow the golden model: per-head [head][token][dim]; a batch adds a
  *    leading axis: Q/O [B][Hq][S][d], K/V [B][Hkv][S][d].  GQA maps query head h to
  *    kv head h / (Hq/Hkv) by address (no KV duplication).
@@ -21,7 +24,9 @@
  *    Arguments are validated on the host before any launch; nothing aborts.
  *  - Kernels bound every internal wait; a wait that gives up records a sticky
  *    device error that gqa_device_check() reports (GQA_ERR_DEVICE_TIMEOUT).
- *  - Thread-safe; the only global state is per-device launch attributes.
+ *  - Thread-safe.  Global state: per-device launch attributes and looked-up
+ *    device addresses, one sticky error word per kernel file and GPU, and the
+ *    no-alloc decode's scratch array (shared by every call on a GPU).
  */
 #ifndef GQA_B200_H_
 #define GQA_B200_H_

@@ -89,9 +89,8 @@ extern "C" int gqa_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 extern "C" int gqa_device_check(gqa_stream_t stream, int* site) {
   if (site) *site = 0;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return GQA_ERR_CUDA;
-  int (*const readers[])(bool) = {error_flag_stages,   error_flag_prefill,   error_flag_prefill7, error_flag_prefill8,
-                                   error_flag_decode, error_flag_decode_tc, error_flag_gemm,     error_flag_kvcache,
-                                   error_flag_peer};
+  int (*const readers[])(bool) = {error_flag_stages, error_flag_prefill, error_flag_decode_tc,
+                                   error_flag_gemm,   error_flag_kvcache, error_flag_peer};
   int first = 0;
   for (auto rd : readers) {  // read and clear every file's word; report the first set one
     const int v = rd(true);
@@ -109,14 +108,4 @@ extern "C" int gqa_prefill_bf16(const void* q, const void* k, const void* v, voi
                                 int kv_head_count, float scale, int flags, gqa_stream_t stream) {
   return launch_prefill(q, k, v, o, cos, sin, B, seq_len, Hq, Hkv, head_dim, kv_head_begin, kv_head_count, scale,
                         flags, stream);
-}
-
-// Diagnostic (not part of the public header): the fused prefill with a clock64 event
-// trace of one CTA written to `trace` (device buffer of 6*128*8 int64).
-extern "C" int gqa_prefill_trace_bf16(const void* q, const void* k, const void* v, void* o, const void* cos,
-                                      const void* sin, int B, int seq_len, int Hq, int Hkv, int head_dim,
-                                      int kv_head_begin, int kv_head_count, float scale, int flags,
-                                      long long* trace, int trace_block, gqa_stream_t stream) {
-  return launch_prefill(q, k, v, o, cos, sin, B, seq_len, Hq, Hkv, head_dim, kv_head_begin, kv_head_count, scale,
-                        flags, stream, trace, trace_block);
 }

@@ -1,246 +1,24 @@
-// decode.cu -- split-KV GQA decode (one query token per sequence) on sm_100a.
+// decode.cu -- host entry points of the split-KV GQA decode (one query token per
+// sequence): argument checks, workspace sizing and the allocation-free variant.
 //
 // out[b,h,:] = softmax_j(q[b,h] . K[b,h/4,j] * scale, j < lens[b]) . V[b,h/4,:,:]
 // This is the single-query-row case of the reference's core
 // (CPU_Baseline/cpu_baseline/attention.py:60-84); the reference has no decode
-// function of its own.  The path is HBM-bound: every K/V byte is read once.
-//
-// Pass 1 (decode_split_kernel): CTA = (key chunk, kv head, sequence), 4 warps.
-//   The chunk's K/V rows are streamed once for all 4 query heads of the group.
-//   Each warp walks 32-key groups: lane = key for q.k (16 x 128-bit loads of its
-//   K row, q broadcast from shared memory), an online softmax per head, then
-//   half-warp = key for p.V (128-bit loads of V rows, p broadcast by shuffle).
-//   The warps' (max, sum, O) states merge in shared memory and the chunk's
-//   partial (O unnormalised, running max m, sum l) goes to the workspace.
-// Pass 2 (decode_combine_kernel): log-sum-exp merge of a sequence's chunks,
-//   O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, written as bf16.
+// function of its own.  The kernels (tcgen05 split pass and log-sum-exp combine)
+// live in decode_sm100.cu.
 #include "common.cuh"
 #include "gqa_internal.h"
-
-#include <cstdlib>
 
 namespace gqa {
 namespace decode {
 
 constexpr int kD = 128;
 constexpr int kG = 4;
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
 constexpr int kDefaultSplit = 2048;
 
-struct Params {
-  const uint16_t* q;
-  const uint16_t* k;
-  const uint16_t* v;
-  const int32_t* lens;
-  const int32_t* q_pos;
-  const uint16_t* cos;
-  const uint16_t* sin;
-  float* ws_o;   // [B][Hq][n_splits][128]
-  float* ws_ml;  // [B][Hq][n_splits][2]
-  uint16_t* out; // [B][Hq][128]
-  int B, Lmax, Hq, Hkv, kv_begin, n_splits, split_len, flags;
-  float scale_log2;
-};
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const Params p) {
-  __shared__ float q_s[kG][kD];
-  __shared__ float m_s[kWarps][kG], l_s[kWarps][kG];
-  __shared__ float o_s[kWarps][kG][kD];
-
-  const int split = blockIdx.x, g = p.kv_begin + static_cast<int>(blockIdx.y), b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int len = min(max(p.lens[b], 0), p.Lmax);
-  const int k0 = split * p.split_len;
-  if (k0 >= len) return;  // chunk past the end of this sequence
-  const int k1 = min(k0 + p.split_len, len);
-
-  // ---- q (4 heads of group g) -> shared fp32, optionally rotated at q_pos[b]
-  {
-    const int h = threadIdx.x >> 5;  // 4 warps <-> 4 heads
-    const uint16_t* qr = p.q + (static_cast<size_t>(b) * p.Hq + g * kG + h) * kD;
-#pragma unroll
-    for (int e = lane; e < kD / 2; e += 32) {
-      float x0 = bf2f_bits(qr[e]), x1 = bf2f_bits(qr[e + kD / 2]);
-      if (p.flags & GQA_FLAG_ROPE_Q) {
-        const size_t row = static_cast<size_t>(min(max(p.q_pos[b], 0), p.Lmax)) * kD;  // table has Lmax+1 rows
-        const float c = bf2f_bits(p.cos[row + e]), s = bf2f_bits(p.sin[row + e]);
-        const float y0 = __fadd_rn(__fmul_rn(x0, c), __fmul_rn(-x1, s));
-        const float y1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
-        x0 = bf2f_bits(f2bf_bits(y0));
-        x1 = bf2f_bits(f2bf_bits(y1));
-      }
-      q_s[h][e] = x0;
-      q_s[h][e + kD / 2] = x1;
-    }
-  }
-  __syncthreads();
-
-  const size_t kv_base = (static_cast<size_t>(b) * p.Hkv + g) * static_cast<size_t>(p.Lmax) * kD;
-  const uint16_t* K = p.k + kv_base;
-  const uint16_t* V = p.v + kv_base;
-  const float sl2 = p.scale_log2;
-
-  float m_run[kG], l_part[kG], o[kG][8];
-#pragma unroll
-  for (int h = 0; h < kG; ++h) {
-    m_run[h] = -INFINITY;
-    l_part[h] = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
-  }
-  const int half = lane >> 4;      // which key of a pair this half-warp handles in p.V
-  const int dchunk = lane & 15;    // 8 dims [8*dchunk, 8*dchunk+8)
-
-  for (int gk = k0 + warp * 32; gk < k1; gk += kWarps * 32) {
-    // ---- q.k, lane = key
-    const int key = gk + lane;
-    float s[kG];
-#pragma unroll
-    for (int h = 0; h < kG; ++h) s[h] = 0.0f;
-    if (key < k1) {
-      const uint4* kr = reinterpret_cast<const uint4*>(K + static_cast<size_t>(key) * kD);
-      uint4 kv[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) kv[c] = __ldg(kr + c);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint32_t w[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float k_lo = bf16_lo(w[e]), k_hi = bf16_hi(w[e]);
-#pragma unroll
-          for (int h = 0; h < kG; ++h) {
-            const float2 qq = *reinterpret_cast<const float2*>(&q_s[h][c * 8 + e * 2]);
-            s[h] = fmaf(qq.x, k_lo, s[h]);
-            s[h] = fmaf(qq.y, k_hi, s[h]);
-          }
-        }
-      }
-    }
-    // ---- online softmax per head over this 32-key group
-    float pk[kG];
-#pragma unroll
-    for (int h = 0; h < kG; ++h) {
-      const float x = key < k1 ? s[h] * sl2 : -INFINITY;
-      const float m_new = fmaxf(m_run[h], warp_max(x));  // finite: the group has >= 1 valid key
-      const float alpha = ex2_approx(m_run[h] - m_new);
-      pk[h] = ex2_approx(x - m_new);
-      l_part[h] = l_part[h] * alpha + pk[h];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[h][e] *= alpha;
-      m_run[h] = m_new;
-    }
-    // ---- p.V, half-warp = key (2 keys per step)
-    const int nk = min(32, k1 - gk);
-    for (int e = 0; e < nk; e += 2) {
-      const int src = e + half;
-      float pp[kG];
-#pragma unroll
-      for (int h = 0; h < kG; ++h) pp[h] = __shfl_sync(0xffffffffu, pk[h], src);
-      if (src < nk) {
-        const uint4 vv = __ldg(reinterpret_cast<const uint4*>(V + static_cast<size_t>(gk + src) * kD) + dchunk);
-        const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float v_lo = bf16_lo(w[q]), v_hi = bf16_hi(w[q]);
-#pragma unroll
-          for (int h = 0; h < kG; ++h) {
-            o[h][2 * q] = fmaf(pp[h], v_lo, o[h][2 * q]);
-            o[h][2 * q + 1] = fmaf(pp[h], v_hi, o[h][2 * q + 1]);
-          }
-        }
-      }
-    }
-  }
-
-  // ---- per-warp reduction: halves hold different keys for the same dims
-#pragma unroll
-  for (int h = 0; h < kG; ++h) {
-    const float lsum = warp_sum(l_part[h]);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[h][e] += __shfl_xor_sync(0xffffffffu, o[h][e], 16);
-    if (lane == 0) {
-      m_s[warp][h] = m_run[h];
-      l_s[warp][h] = lsum;
-    }
-    if (lane < 16) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o_s[warp][h][dchunk * 8 + e] = o[h][e];
-    }
-  }
-  __syncthreads();
-
-  // ---- merge the 4 warps; thread = (head, 32 dims)
-  {
-    const int h = threadIdx.x >> 5;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w][h]);
-    float L = 0.0f, sc[kWarps];
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      sc[w] = (m_s[w][h] == -INFINITY) ? 0.0f : ex2_approx(m_s[w][h] - M);
-      L += l_s[w][h] * sc[w];
-    }
-    const size_t slot = (static_cast<size_t>(b) * p.Hq + g * kG + h) * p.n_splits + split;
-#pragma unroll
-    for (int e = lane; e < kD; e += 32) {
-      float acc = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) acc += o_s[w][h][e] * sc[w];
-      p.ws_o[slot * kD + e] = acc;
-    }
-    if (lane == 0) {
-      p.ws_ml[slot * 2 + 0] = M;
-      p.ws_ml[slot * 2 + 1] = L;
-    }
-  }
-}
-
-// grid = (kv_count*4 heads, B); block = 128 threads (thread = dim).
-__global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
-  const int b = blockIdx.y;
-  const int h = p.kv_begin * kG + static_cast<int>(blockIdx.x);
-  const int len = min(max(p.lens[b], 0), p.Lmax);
-  const int ns = (len + p.split_len - 1) / p.split_len;
-  const size_t base = (static_cast<size_t>(b) * p.Hq + h) * p.n_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, p.ws_ml[(base + s) * 2]);
-  float L = 0.0f, acc = 0.0f;
-  for (int s = 0; s < ns; ++s) {
-    const float m = p.ws_ml[(base + s) * 2];
-    const float w = (m == -INFINITY) ? 0.0f : ex2_approx(m - M);
-    L += p.ws_ml[(base + s) * 2 + 1] * w;
-    acc += p.ws_o[(base + s) * kD + threadIdx.x] * w;
-  }
-  p.out[(static_cast<size_t>(b) * p.Hq + h) * kD + threadIdx.x] = f2bf_bits(L > 0.0f ? acc / L : 0.0f);
-}
-
 inline int effective_split(int max_len, int split_len) {
-  if (split_len > 0) return split_len;
-  return kDefaultSplit;
-}
-
-// The tcgen05 split-KV kernel (decode_sm100.cu) is the default; GQA_DECODE_CUDA_CORES=1
-// selects the CUDA-core kernel above (kept as a cross-check of the tensor-core path).
-inline bool use_tensor_core_decode() {
-  static const bool tc = [] {
-    const char* e = getenv("GQA_DECODE_CUDA_CORES");
-    return !(e && e[0] == '1');
-  }();
-  return tc;
+  (void)max_len;
+  return split_len > 0 ? split_len : kDefaultSplit;
 }
 
 }  // namespace decode
@@ -277,35 +55,8 @@ extern "C" int gqa_decode_bf16(const void* q, const void* kcache, const void* vc
   const int ns = (max_len + sl - 1) / sl;
   if (ns > 65535 || B > 65535) return GQA_ERR_UNSUPPORTED;
 
-  Params p;
-  p.q = static_cast<const uint16_t*>(q);
-  p.k = static_cast<const uint16_t*>(kcache);
-  p.v = static_cast<const uint16_t*>(vcache);
-  p.lens = lens;
-  p.q_pos = q_pos;
-  p.cos = static_cast<const uint16_t*>(cos);
-  p.sin = static_cast<const uint16_t*>(sin);
-  float* ws = static_cast<float*>(workspace);
-  const size_t n_slots = static_cast<size_t>(B) * Hq * ns;
-  p.ws_o = ws;
-  p.ws_ml = ws + n_slots * kD;
-  p.out = static_cast<uint16_t*>(o);
-  p.B = B;
-  p.Lmax = max_len;
-  p.Hq = Hq;
-  p.Hkv = Hkv;
-  p.kv_begin = kv_head_begin;
-  p.n_splits = ns;
-  p.split_len = sl;
-  p.flags = flags;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  if (use_tensor_core_decode())
-    return launch_decode_tc(q, kcache, vcache, lens, q_pos, cos, sin, o, ws, B, max_len, Hq, Hkv, kv_head_begin,
-                            kv_head_count, sl, ns, scale, flags, stream);
-  decode_split_kernel<<<dim3(ns, kv_head_count, B), kThreads, 0, stream>>>(p);
-  if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
-  decode_combine_kernel<<<dim3(kv_head_count * kG, B), kD, 0, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+  return launch_decode_tc(q, kcache, vcache, lens, q_pos, cos, sin, o, static_cast<float*>(workspace), B, max_len, Hq,
+                          Hkv, kv_head_begin, kv_head_count, sl, ns, scale, flags, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -416,6 +167,3 @@ extern "C" int gqa_decode_bf16_noalloc(const void* q, const void* kcache, const 
                          Hkv, head_dim, kv_head_begin, kv_head_count, split_len, scale, flags, stream);
 }
 
-namespace gqa {
-GQA_ERROR_FLAG_ACCESSOR(error_flag_decode)
-}  // namespace gqa

@@ -387,12 +387,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   if (p.scatter_rows > 0 && threadIdx.x == 0) {
-    // the last CTA to finish tells every destination that its rows are complete
+    // The last CTA to finish tells every destination that its rows are complete, unless
+    // a wait of this grid gave up (a CTA that failed skipped its stores): then no flag is
+    // raised, the owners' bounded waits expire and they report the timeout too, instead
+    // of reducing slots that still hold the previous step's rows.  The fences order every
+    // CTA's error record (made before the block barrier above) before its arrival.
+    __threadfence();
     if (atomicAdd(p.sig_counter, 1u) + 1u == gridDim.x) {
+      __threadfence();
       *p.sig_counter = 0u;
       __threadfence_system();
-      for (int q = 0; q < p.n_dest; ++q)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag_at(p, q)), "r"(p.sig_epoch) : "memory");
+      if (!error_pending())
+        for (int q = 0; q < p.n_dest; ++q)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag_at(p, q)), "r"(p.sig_epoch) : "memory");
     }
   }
   if (warp == 1) {
@@ -715,9 +722,13 @@ extern "C" int gqa_o_proj_rows_bf16(const void* attn, const void* wo, void* out,
 namespace gqa {
 // o_proj (B = 1) whose fp32 rows go straight to their owners: row m to dst[m / (S / world)]
 // + (m % (S / world)) * N, then the grid's last CTA raises flags[q] = epoch for every q.
+// `local` is a buffer of this GPU holding at least S / world x N fp32.
 int launch_o_proj_scatter(const void* attn, const void* wo, int S, int Hq, int N, int ldw, float* const* dst,
-                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, cudaStream_t stream) {
-  if (!attn || !wo || !dst || !flags || !counter || world < 1 || world > gemm::kMaxDest) return GQA_ERR_INVALID_ARGUMENT;
+                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, float* local,
+                          cudaStream_t stream) {
+  if (!attn || !wo || !dst || !flags || !counter || !local || world < 1 || world > gemm::kMaxDest)
+    return GQA_ERR_INVALID_ARGUMENT;
+  if (bad16(local)) return GQA_ERR_MISALIGNED;
   if (S <= 0 || Hq <= 0 || N <= 0 || S % world || (S / world) % gemm::kBM || N % 256) return GQA_ERR_UNSUPPORTED;
   if (ldw < Hq * 128 || ldw % 8) return GQA_ERR_INVALID_ARGUMENT;
   if (bad16(attn) || bad16(wo)) return GQA_ERR_MISALIGNED;
@@ -742,8 +753,10 @@ int launch_o_proj_scatter(const void* attn, const void* wo, int S, int Hq, int N
   L.reg[0] = gemm::Region{0, N, 0, 0};
   L.w[0] = wo;
   L.ldw[0] = ldw;
-  // the staging / TMA-store map is built but unused in scatter mode: any valid fp32 view
-  L.c[0] = dst[0];
+  // The staging / TMA-store map is built but never used in scatter mode.  It covers the
+  // caller's local buffer (at least S / world rows of N fp32), so no tensor map of the
+  // multi-GPU path describes another GPU's memory.
+  L.c[0] = local;
   L.c_dims[0][0] = N;
   L.c_dims[0][1] = S / world;
   L.c_dims[0][2] = 1;
@@ -796,4 +809,21 @@ extern "C" int gqa_cast_f32_bf16(const void* src, void* dst, long long n, gqa_st
 
 namespace gqa {
 GQA_ERROR_FLAG_ACCESSOR(error_flag_gemm)
+
+int gemm_error_word(const int** out) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<const int*> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return GQA_ERR_UNSUPPORTED;
+  const int* a = cache[dev].load(std::memory_order_acquire);
+  if (a == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_gqa_dev_error) != cudaSuccess || addr == nullptr) return GQA_ERR_CUDA;
+    a = static_cast<const int*>(addr);
+    cache[dev].store(a, std::memory_order_release);
+  }
+  *out = a;
+  return GQA_OK;
+}
 }  // namespace gqa

@@ -39,9 +39,6 @@ int ensure_smem_attr(F func, int bytes, std::atomic<uint64_t>& done_mask) {
 // Per-file device error words (see GQA_ERROR_FLAG_ACCESSOR): value, optionally cleared.
 int error_flag_stages(bool clear);
 int error_flag_prefill(bool clear);
-int error_flag_prefill7(bool clear);
-int error_flag_prefill8(bool clear);
-int error_flag_decode(bool clear);
 int error_flag_decode_tc(bool clear);
 int error_flag_gemm(bool clear);
 int error_flag_kvcache(bool clear);
@@ -49,18 +46,15 @@ int error_flag_peer(bool clear);
 
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
-                   cudaStream_t stream, long long* trace = nullptr, int trace_block = -1);
-
-int launch_prefill7(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B,
-                    int S, int Hq, int Hkv, int kv_begin, int kv_count, float scale, int flags, cudaStream_t stream,
-                    long long* trace = nullptr, int trace_block = -1);
-
-int launch_prefill8(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B,
-                    int S, int Hq, int Hkv, int kv_begin, int kv_count, float scale, int flags, cudaStream_t stream,
-                    long long* trace = nullptr, int trace_block = -1);
+                   cudaStream_t stream);
 
 int launch_o_proj_scatter(const void* attn, const void* wo, int S, int Hq, int N, int ldw, float* const* dst,
-                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, cudaStream_t stream);
+                          uint32_t* const* flags, int world, uint32_t* counter, uint32_t epoch, float* local,
+                          cudaStream_t stream);
+
+// Device address of the GEMM file's sticky error word on the current device (looked up
+// once per device), so kernels of other files can refuse to signal after a failed GEMM.
+int gemm_error_word(const int** out);
 
 int launch_decode_tc(const void* q, const void* kcache, const void* vcache, const int32_t* lens, const int32_t* q_pos,
                      const void* cos, const void* sin, void* o, float* ws, int B, int max_len, int Hq, int Hkv,

@@ -75,10 +75,12 @@ __device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, int site) {
   }
 }
 
-// This rank's partial (written by the preceding GEMM launch) is ready.
-__global__ void signal_kernel(uint32_t* flag, uint32_t epoch) {
+// This rank's partial (written by the preceding GEMM launch) is ready.  Not raised when
+// that GEMM or an earlier exchange kernel on this GPU gave up a wait: the peers' bounded
+// waits then expire and they report the timeout too, instead of summing a stale partial.
+__global__ void signal_kernel(uint32_t* flag, uint32_t epoch, const int* gemm_error) {
   __threadfence_system();
-  st_release_sys(flag, epoch);
+  if (*reinterpret_cast<const volatile int*>(gemm_error) == 0 && !error_pending()) st_release_sys(flag, epoch);
 }
 
 __global__ void __launch_bounds__(kThreads) tp_reduce_kernel(const Params prm) {
@@ -142,7 +144,9 @@ __global__ void __launch_bounds__(kThreads) tp_reduce_kernel(const Params prm) {
     if (arrived == gridDim.x) {
       *prm.counter = 0u;
       __threadfence_system();
-      if (ok_s) st_release_sys(prm.p.done[prm.rank], prm.epoch);
+      // every block's wait result is recorded before its arrival: one that gave up
+      // leaves the error word set, and then no block is announced
+      if (ok_s && !error_pending()) st_release_sys(prm.p.done[prm.rank], prm.epoch);
     }
   }
 }
@@ -250,7 +254,7 @@ __global__ void __launch_bounds__(kThreads) tp_reduce_push_kernel(const PushPara
     if (atomicAdd(prm.counter, 1u) + 1u == gridDim.x) {
       *prm.counter = 0u;
       __threadfence_system();
-      if (ok_s)
+      if (ok_s && !error_pending())
         for (int q = 0; q < prm.world; ++q) st_release_sys(prm.flag_b[q], prm.epoch);
     }
   }
@@ -334,8 +338,11 @@ extern "C" int gqa_tp_reduce_gather_bf16(const void* const* bases, int world, in
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int* gemm_err = nullptr;
+  const int rc = gemm_error_word(&gemm_err);
+  if (rc != GQA_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  signal_kernel<<<1, 1, 0, st>>>(prm.p.ready[rank], epoch);
+  signal_kernel<<<1, 1, 0, st>>>(prm.p.ready[rank], epoch, gemm_err);
   if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
   tp_reduce_kernel<<<2 * sms, kThreads, 0, st>>>(prm);
   if (cudaGetLastError() != cudaSuccess) return GQA_ERR_CUDA;
@@ -388,7 +395,7 @@ extern "C" int gqa_tp_o_proj_exchange_bf16(const void* attn, const void* wo, int
   pp.epoch = epoch;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = launch_o_proj_scatter(attn, wo, S, Hq, N, ldw, dst, flag_a, world, reinterpret_cast<uint32_t*>(mflags + 132),
-                                 epoch, st);
+                                 epoch, reinterpret_cast<float*>(mine), st);
   if (rc != GQA_OK) return rc;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);

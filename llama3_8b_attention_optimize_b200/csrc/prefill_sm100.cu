@@ -42,8 +42,6 @@
 // so p <= 2^16: with |v| < 2^16 and at most 2^17 keys, O stays below 2^49 (fp32-safe).
 #include <cuda.h>
 
-#include <cstdlib>
-
 #include "attn_common.cuh"
 #include "common.cuh"
 #include "gqa_internal.h"
@@ -137,18 +135,7 @@ struct Params {
   float scale_log2;
   const uint16_t* cos;  // [>= S][128] bf16 (cat(freqs, freqs) layout)
   const uint16_t* sin;
-  long long* trace;  // diagnostic event trace of one CTA (nullptr = off)
-  int trace_block;
 };
-
-// Diagnostic trace: clock64 stamps [role][iteration][event] for CTA trace_block.
-constexpr int kTraceIters = 128;
-constexpr int kTraceRoles = 6;
-constexpr int kTraceEv = 8;
-#define PF_TRACE(role, it, ev)                                                                        \
-  do {                                                                                                \
-    if (kTrace && tr) tr[((role) * kTraceIters + min((it), kTraceIters - 1)) * kTraceEv + (ev)] = clock64(); \
-  } while (0)
 
 __device__ __forceinline__ uint32_t colS(int t) { return static_cast<uint32_t>(t * 128); }
 __device__ __forceinline__ uint32_t colO(int t) { return static_cast<uint32_t>(256 + t * 128); }
@@ -187,7 +174,6 @@ struct Unit {
   int p0, n_kv, zq, zk;
 };
 
-template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -272,8 +258,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmemPtr);
-  long long* tr = (kTrace && static_cast<int>(blockIdx.x) == p.trace_block) ? p.trace : nullptr;
-  if (threadIdx.x == 0) PF_TRACE(5, 0, 0);
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ TMA producer
@@ -288,7 +272,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit x = decode(u);
         // The Q tiles are reused once the previous unit's last QK^T is done.
         if (uc > 0 && !(ok = mbar_wait(bar(B_QEMPTY), (uc - 1) & 1, SITE_PRODUCER))) break;
-        PF_TRACE(5, uc, 1);
         for (int t = 0; t < 2; ++t) {
           const uint32_t dst = sbase + kOffQ + t * kTileBytes;
           mbar_expect_tx(bar(B_QFULL + t), kTileBytes);
@@ -318,7 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(bar(B_KVFULL + s), kTileBytes);
           tma_load_3d(dst, map, bar(B_KVFULL + s), 0, j * kBN, x.zk);
           tma_load_3d(dst + kHalf, map, bar(B_KVFULL + s), 64, j * kBN, x.zk);
-          PF_TRACE(0, j, is_v ? 1 : 0);
           ++L;
         }
         ++uc;
@@ -385,11 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         // Q of this unit ready, and the S buffers released by the previous unit's softmax
         ok = mbar_wait_spin(bar(B_QREADY + 0), uc & 1, SITE_MMA) && mbar_wait_spin(bar(B_QREADY + 1), uc & 1, SITE_MMA);
-        PF_TRACE(5, uc, 6);
         ok = ok && wait_k(0) &&
              (Gb == 0 || (mbar_wait_spin(bar(sfree_bar(0)), (Gb - 1) & 1u, SITE_MMA) &&
                           mbar_wait_spin(bar(sfree_bar(1)), (Gb - 1) & 1u, SITE_MMA)));
-        PF_TRACE(5, uc, 7);
         if (!ok) break;
         {
           const int sk = static_cast<int>((L + load_idx_k(0)) % kStages);
@@ -403,7 +383,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int j = 0; ok && j < n; ++j) {
           const uint32_t g = Gb + j;
-          PF_TRACE(1, g, 0);
           const int sk = static_cast<int>((L + load_idx_k(j + 1)) % kStages);  // used when j + 1 < n
           const uint32_t iv = L + load_idx_v(j, n);
           const int sv = static_cast<int>(iv % kStages);
@@ -416,15 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               issue_qk(0, sk);
               umma_commit(bar(B_SFULL + 0));
             }
-            PF_TRACE(1, g, 1);
             ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
                  mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
             if (!ok) break;
-            PF_TRACE(1, g, 2);
             tc_fence_after();
             issue_pv(0, sv, j > 0 ? 1u : 0u);
             umma_commit(bar(B_PVDONE + 0));
-            PF_TRACE(1, g, 3);
             if (j + 1 < n) {
               ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
               if (!ok) break;
@@ -434,26 +410,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_commit(bar(B_KVEMPTY + sk));
               if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
             }
-            PF_TRACE(1, g, 4);
             ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
             if (!ok) break;
-            PF_TRACE(1, g, 5);
             tc_fence_after();
             issue_pv(1, sv, j > 0 ? 1u : 0u);
             umma_commit(bar(B_PVDONE + 1));
             umma_commit(bar(B_KVEMPTY + sv));
-            PF_TRACE(1, g, 7);
             continue;
           }
           if (j + 1 < n) {
             // next S as soon as the softmax warps hold S(j) in registers
             ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(0)), g & 1u, SITE_MMA);
             if (!ok) break;
-            PF_TRACE(1, g, 1);
             tc_fence_after();
             issue_qk(0, sk);
             umma_commit(bar(B_SFULL + 0));
-            PF_TRACE(1, g, 2);
             if (kMmaOrder == 1) {
               ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
               if (!ok) break;
@@ -463,26 +434,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(bar(B_SFULL + 1));
             umma_commit(bar(B_KVEMPTY + sk));
             if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
-            PF_TRACE(1, g, 3);
           }
           ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
                mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
           if (!ok) break;
-          PF_TRACE(1, g, 4);
           tc_fence_after();
           issue_pv(0, sv, j > 0 ? 1u : 0u);
           umma_commit(bar(B_PVDONE + 0));
-          PF_TRACE(1, g, 5);
           if (kMmaOrder == 1) {
             ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
             if (!ok) break;
             tc_fence_after();
           }
-          PF_TRACE(1, g, 6);
           issue_pv(1, sv, j > 0 ? 1u : 0u);
           umma_commit(bar(B_PVDONE + 1));
           umma_commit(bar(B_KVEMPTY + sv));
-          PF_TRACE(1, g, 7);
         }
         L += 2 * n;
         Gb += n;
@@ -504,7 +470,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int u = unit_of(i);
       if (u < 0) continue;
       const Unit x = decode(u);
-      if (tid == 0) PF_TRACE(4, uc, 0);
       if (rope_k) {
         for (int j = 0; j < x.n_kv; ++j) {
           const uint32_t ii = L + load_idx_k(j);
@@ -551,14 +516,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rotates 4 of the row's 8 chunk pairs), then release it to the tensor core.
     auto prepare_q = [&](const Unit& y, int parity, int unit_no) {
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_QFULL + t), parity, SITE_SOFTMAX));
-      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, unit_no, 2);
       const int pos = y.p0 + t * kRowsPerHead + (r & (kRowsPerHead - 1));
       if (ok && rope_q && pos < p.S)
         rope_row_smem_part(smem + kOffQ + t * kTileBytes, kHalf, r, p.cos + static_cast<size_t>(pos) * kD,
                            p.sin + static_cast<size_t>(pos) * kD, 4 * h);
       fence_proxy_async_smem();
       warp_arrive(bar(B_QREADY + t));
-      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, unit_no, 3);
     };
     {
       const int u0 = unit_of(0);
@@ -592,7 +555,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + t), gi & 1u, SITE_SOFTMAX));
-        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 0);
         uint32_t s0[32], s1[32];
         if (ok) {
           tc_fence_after();
@@ -632,7 +594,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         xchg[h * 128 + r] = fmaxf(mx0, mx1);
         named_bar_sync(bar_x, 256);
         const float m_tile = fmaxf(fmaxf(mx0, mx1), xchg[(1 - h) * 128 + r]) * sl2;
-        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 1);
         const float m_new = fmaxf(m_run, m_tile);
         const bool need = m_new > m_run + kRescaleLog2;
         const float m_use = need ? m_new : m_run;
@@ -644,7 +605,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // iteration loaded S and exchanged the row max, so the wait is normally short, and
         // p can then go to shared memory as it is computed.
         if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), (gi - 1) & 1u, SITE_SOFTMAX));
-        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 2);
         float2 sum = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
         if (ok) {
           const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-moff, -moff);
@@ -676,7 +636,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l_run = l_run * alpha + ((sum.x + sum.y) + (sumb.x + sumb.y));
         m_run = m_use;
-        if (r == 0 && h == 0) PF_TRACE(2 + t, gi, 3);
       }
 
       // The next unit's Q was loaded once this unit's last QK^T finished: rotate and
@@ -685,7 +644,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- epilogue: O / l -> bf16 -> P_t's buffer (free once the last PV is done) ->
       // one TMA store per 64-dim half of the tile
       const uint32_t last = Gb + n_kv - 1;
-      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, uc, 4);
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + t), last & 1u, SITE_EPILOGUE));
       named_bar_sync(bar_free, 256);
       xchg[h * 128 + r] = l_run;
@@ -721,7 +679,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_commit();
         store_pending = true;
       }
-      if (r == 0 && h == 0 && t == 0) PF_TRACE(5, uc, 5);
       Gb += n_kv;
       ++uc;
     }
@@ -740,23 +697,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace prefill
 
 // ------------------------------------------------------------------ host side
-// Which fused kernel serves gqa_prefill_bf16: 6 = this file's (two warpgroups per Q tile,
-// P through shared memory), 7 = prefill7_sm100.cu (one thread per row, P in TMEM),
-// 8 = prefill8_sm100.cu (four lanes per row, P in TMEM).  GQA_PREFILL_KERNEL=6|7|8
-// overrides the default.
-int prefill_variant() {
-  static const int v = [] {
-    const char* e = getenv("GQA_PREFILL_KERNEL");
-    if (e && e[0] == '7') return 7;
-    if (e && e[0] == '8') return 8;
-    return 6;
-  }();
-  return v;
-}
-
 int launch_prefill(const void* q, const void* k, const void* v, void* o, const void* cos, const void* sin, int B, int S,
                    int Hq, int Hkv, int head_dim, int kv_begin, int kv_count, float scale, int flags,
-                   cudaStream_t stream, long long* trace, int trace_block) {
+                   cudaStream_t stream) {
   using namespace prefill;
   if (!q || !k || !v || !o) return GQA_ERR_INVALID_ARGUMENT;
   if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0) return GQA_ERR_INVALID_ARGUMENT;
@@ -767,12 +710,6 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   if ((flags & (GQA_FLAG_ROPE_Q | GQA_FLAG_ROPE_K)) && (!cos || !sin)) return GQA_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return GQA_ERR_MISALIGNED;
   if ((flags & (GQA_FLAG_ROPE_Q | GQA_FLAG_ROPE_K)) && (!aligned16(cos) || !aligned16(sin))) return GQA_ERR_MISALIGNED;
-  if (prefill_variant() == 7)
-    return launch_prefill7(q, k, v, o, cos, sin, B, S, Hq, Hkv, kv_begin, kv_count, scale, flags, stream, trace,
-                           trace_block);
-  if (prefill_variant() == 8)
-    return launch_prefill8(q, k, v, o, cos, sin, B, S, Hq, Hkv, kv_begin, kv_count, scale, flags, stream, trace,
-                           trace_block);
   const long long n_qblocks = (S + kPosPerCta - 1) / kPosPerCta;
   const long long n_units = n_qblocks * B * kv_count;
   if (n_units > 0x7FFFFFFFLL || static_cast<long long>(B) * Hq > 0x7FFFFFFFLL) return GQA_ERR_UNSUPPORTED;
@@ -786,17 +723,14 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   if ((rc = make_tmap_3d_bf16(&tmO, o, kD, S, static_cast<long long>(B) * Hq, 64, kRowsPerHead, kG)) != GQA_OK)
     return rc;
 
-  static std::atomic<uint64_t> attr_done{0}, attr_done_tr{0};
-  if ((rc = ensure_smem_attr(prefill_kernel<false>, kSmemBytes, attr_done)) != GQA_OK) return rc;
-  if (trace && (rc = ensure_smem_attr(prefill_kernel<true>, kSmemBytes, attr_done_tr)) != GQA_OK) return rc;
+  static std::atomic<uint64_t> attr_done{0};
+  if ((rc = ensure_smem_attr(prefill_kernel, kSmemBytes, attr_done)) != GQA_OK) return rc;
   // The register split assumes the kernel was compiled to kRegsLaunch registers per thread.
   static std::atomic<int> regs_ok{0};
   if (regs_ok.load(std::memory_order_acquire) == 0) {
-    cudaFuncAttributes fa, fb;
-    if (cudaFuncGetAttributes(&fa, prefill_kernel<false>) != cudaSuccess ||
-        cudaFuncGetAttributes(&fb, prefill_kernel<true>) != cudaSuccess)
-      return GQA_ERR_CUDA;
-    regs_ok.store(fa.numRegs == kRegsLaunch && fb.numRegs == kRegsLaunch ? 1 : -1, std::memory_order_release);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, prefill_kernel) != cudaSuccess) return GQA_ERR_CUDA;
+    regs_ok.store(fa.numRegs == kRegsLaunch ? 1 : -1, std::memory_order_release);
   }
   if (regs_ok.load(std::memory_order_acquire) < 0) return GQA_ERR_UNSUPPORTED;
   int dev = 0, sms = 148;
@@ -815,13 +749,8 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   p.scale_log2 = scale * 1.4426950408889634f;
   p.cos = static_cast<const uint16_t*>(cos);
   p.sin = static_cast<const uint16_t*>(sin);
-  p.trace = trace;
-  p.trace_block = trace_block;
   const int grid = static_cast<int>(n_units < sms ? n_units : sms);
-  if (trace)
-    prefill_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
-  else
-    prefill_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
+  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 

@@ -4,17 +4,20 @@ stage dumps.
 The reference turns its golden-model dumps into one-word-per-line hex files for the
 Verilog test benches (A_attention_integration_final_v5/scripts/
 prepare_attention_fpga_slice_vectors.py).  This module writes the same files, with the
-same names, word order and checks, from this package's GPU stage kernels:
+same names, word order and format, from this package's GPU stage kernels.  The file
+format, names and manifest fields are the reference's (the test benches read them); the
+readers and checks are this module's own, and raise VectorFileError (a ValueError):
 
 =============================  ====================================================
 function                       reference (prepare_attention_fpga_slice_vectors.py)
 =============================  ====================================================
 ``SHAPES``, ``NPY_TO_HEX``     :20-38 (slice shapes and file names)
-``load_real_npy``              :49-72 (LFS pointer / shape / dtype / finite / bf16-exact checks)
+``load_real_npy``              :49-72 (the same checks: LFS pointer, shape, dtype, finite, bf16)
 ``bf16_words``                 :75-77
-``read_hex``                   :80-97 (blank lines skipped, <= 0xFFFF, exact count)
+``read_hex``                   :80-97 (the same format: blank lines skipped, 16-bit words,
+                               exact count)
 ``write_hex``                  :100-103 (``%04X`` + LF)
-``assert_existing_hex_matches`` :106-119
+``assert_existing_hex_matches`` :106-119 (same purpose)
 ``emit_fpga_slice``            :171-249 (hex files, sin/cos tables, manifest)
 =============================  ====================================================
 
@@ -32,6 +35,7 @@ from __future__ import annotations
 
 import hashlib
 import json
+import re
 from pathlib import Path
 
 import numpy as np
@@ -62,32 +66,46 @@ ROM_TABLES = ("sin_bf16.hex", "cos_bf16.hex")
 MANIFEST_NAME = "attention_fpga_slice_manifest.json"
 
 
+class VectorFileError(ValueError):
+    """A golden tensor or hex vector file that the test benches cannot use."""
+
+
 def sha256(path) -> str:
-    digest = hashlib.sha256()
-    with open(path, "rb") as handle:
-        for block in iter(lambda: handle.read(1 << 20), b""):
-            digest.update(block)
-    return digest.hexdigest()
+    """Hex SHA-256 digest of a file (the manifest's checksum; vector files are small)."""
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+
+
+_LFS_SIGNATURE = b"version https://git-lfs.github.com/spec/v1"
 
 
 def load_real_npy(path, shape: tuple) -> np.ndarray:
-    """Load a golden .npy holding bf16-exact values in fp32 storage; raise on an LFS
-    pointer, a wrong shape or dtype, non-finite values or non-bf16 values."""
+    """Load one golden tensor: float32 storage holding bf16 values of the given shape.
+
+    Every problem found is reported at once in one VectorFileError: a Git LFS placeholder
+    instead of the array, a shape or dtype other than expected, and (on float32 data)
+    the number of NaN/Inf words and of words whose low 16 bits are set (values a bf16
+    word cannot hold).  The checks on the words are one pass over their bit patterns."""
     path = Path(path)
-    if not path.is_file():
-        raise FileNotFoundError(f"missing golden tensor: {path}")
-    if path.read_bytes()[:64].startswith(b"version https://git-lfs.github.com/spec/v1"):
-        raise RuntimeError(f"{path} is only a Git LFS pointer, not array data")
-    array = np.load(path, allow_pickle=False)
-    if array.shape != tuple(shape):
-        raise ValueError(f"{path.name}: expected shape {tuple(shape)}, got {array.shape}")
-    if array.dtype != np.float32:
-        raise TypeError(f"{path.name}: expected float32 storage, got {array.dtype}")
-    if not np.isfinite(array).all():
-        raise ValueError(f"{path.name}: NaN or Inf is not permitted")
-    if np.any(array.view(np.uint32) & np.uint32(0xFFFF)):
-        raise ValueError(f"{path.name}: values are not already exact BF16 boundary values")
-    return array
+    with path.open("rb") as fh:  # FileNotFoundError for a missing tensor
+        if fh.read(len(_LFS_SIGNATURE)) == _LFS_SIGNATURE:
+            raise VectorFileError(f"{path}: Git LFS placeholder; fetch the LFS object before converting")
+    arr = np.load(path, allow_pickle=False)
+    problems = []
+    if arr.shape != tuple(shape):
+        problems.append(f"shape {arr.shape}, want {tuple(shape)}")
+    if arr.dtype != np.float32:
+        problems.append(f"dtype {arr.dtype}, want float32")
+    else:
+        bits = np.ascontiguousarray(arr).view(np.uint32)
+        n_nonfinite = int(np.count_nonzero((bits & 0x7F800000) == 0x7F800000))
+        n_wide = int(np.count_nonzero(bits & 0xFFFF))
+        if n_nonfinite:
+            problems.append(f"{n_nonfinite} NaN/Inf words")
+        if n_wide:
+            problems.append(f"{n_wide} words that are not bf16 (low 16 bits set)")
+    if problems:
+        raise VectorFileError(f"{path.name}: " + "; ".join(problems))
+    return arr
 
 
 def bf16_words(x) -> np.ndarray:
@@ -105,27 +123,25 @@ def bf16_words(x) -> np.ndarray:
     return (bits >> np.uint32(16)).astype(np.uint16)
 
 
+_HEX_WORD = re.compile(r"0*[0-9A-Fa-f]{1,4}")  # a 16-bit word (leading zeros allowed)
+
+
 def read_hex(path, expected_words: int) -> np.ndarray:
-    """One 16-bit hex word per line (blank lines skipped); exactly `expected_words`."""
+    """Parse a hex vector file: one 16-bit word per non-blank line (CR/LF, any case).
+
+    A missing file raises FileNotFoundError; a line that is not a 16-bit hex word, or a
+    word count other than `expected_words`, raises VectorFileError naming the file (and
+    the first offending line)."""
     path = Path(path)
-    if not path.is_file():
-        raise FileNotFoundError(f"missing HEX file: {path}")
-    words = []
-    with path.open("r", encoding="ascii") as handle:
-        for line_number, line in enumerate(handle, 1):
-            text = line.strip()
-            if not text:
-                continue
-            try:
-                value = int(text, 16)
-            except ValueError as exc:
-                raise ValueError(f"{path}:{line_number}: invalid HEX {text!r}") from exc
-            if not 0 <= value <= 0xFFFF:
-                raise ValueError(f"{path}:{line_number}: value is wider than BF16")
-            words.append(value)
-    if len(words) != expected_words:
-        raise ValueError(f"{path}: expected {expected_words} words, got {len(words)}")
-    return np.asarray(words, dtype=np.uint16)
+    text = path.read_text(encoding="ascii")
+    lines = [(no, ln.strip()) for no, ln in enumerate(text.splitlines(), 1)]
+    tokens = [(no, tok) for no, tok in lines if tok]
+    for no, tok in tokens:
+        if not _HEX_WORD.fullmatch(tok):
+            raise VectorFileError(f"{path}, line {no}: {tok!r} is not a 16-bit hex word")
+    if len(tokens) != expected_words:
+        raise VectorFileError(f"{path}: {len(tokens)} words, want {expected_words}")
+    return np.array([int(tok, 16) for _, tok in tokens], dtype=np.uint16)
 
 
 def write_hex(path, words) -> None:
@@ -137,17 +153,18 @@ def write_hex(path, words) -> None:
 
 
 def assert_existing_hex_matches(existing, generated, logical_name: str) -> None:
-    """If `existing` is a file, it must hold exactly `generated` (first mismatch raised)."""
+    """When `existing` names a file, it must hold exactly the `generated` words;
+    otherwise RuntimeError reports how many words differ and where the first one is."""
     existing = Path(existing)
     if not existing.is_file():
         return
-    flat = np.asarray(generated, dtype=np.uint16).reshape(-1)
-    committed = read_hex(existing, int(flat.size))
-    mismatch = np.flatnonzero(committed != flat)
-    if mismatch.size:
-        i = int(mismatch[0])
-        raise RuntimeError(f"{logical_name}: generated words disagree with {existing} at word {i}: "
-                           f"generated={int(flat[i]):04X}, existing={int(committed[i]):04X}")
+    gen = np.asarray(generated, dtype=np.uint16).ravel()
+    old = read_hex(existing, gen.size)
+    diff = old != gen
+    if diff.any():
+        first = int(diff.argmax())
+        raise RuntimeError(f"{logical_name}: {int(diff.sum())} of {gen.size} words differ from {existing}, "
+                           f"first at word {first} (now {gen[first]:04X}, file has {old[first]:04X})")
 
 
 def _bf16_rne(x: np.ndarray) -> np.ndarray:

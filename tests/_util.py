@@ -1,6 +1,9 @@
 """Shared helpers for the test suite (seeded inputs, bf16 word views, ulp metrics)."""
 from __future__ import annotations
 
+import json
+import os
+
 import numpy as np
 import torch
 
@@ -45,3 +48,18 @@ def bf16_ulp_of(x: np.ndarray) -> np.ndarray:
     ax = np.maximum(np.abs(x).astype(np.float32), np.float32(2.0 ** -126))
     e = np.floor(np.log2(ax))
     return np.exp2(e - 7).astype(np.float32)
+
+
+def report_ulps(name: str, hists) -> dict:
+    """Print the mean of ulp histograms (kernel output vs the correctly rounded exact
+    value) under `name` and, when GQA_PARITY_REPORT names a file, append it there as a
+    JSON line.  `hists` is one ulp_histogram dict or a list of them (equal weights)."""
+    hists = [hists] if isinstance(hists, dict) else list(hists)
+    hist = {k: sum(h[k] for h in hists) / len(hists) for k in ("0", "1", "2", ">2")}
+    hist["max"] = max(h["max"] for h in hists)
+    print(f"ulp histogram {name}: {hist}")
+    path = os.environ.get("GQA_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"check": name, "ulp": hist}) + "\n")
+    return hist

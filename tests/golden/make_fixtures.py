@@ -1,8 +1,10 @@
 """Regenerate the golden fixtures under tests/golden/ from the reference repository.
 
-Run in the build container (the reference is mounted there read-only):
+Run where a checkout of the reference repository is available (read-only is fine):
 
-    python tests/golden/make_fixtures.py [--reference /root/reference]
+    python tests/golden/make_fixtures.py --reference <path to the reference checkout>
+
+(or set GQA_REFERENCE_DIR instead of passing --reference).
 
 Writes:
 
@@ -165,8 +167,11 @@ def make_layer(ref: str) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GQA_REFERENCE_DIR"),
+                    help="path of the reference checkout (default: $GQA_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference or GQA_REFERENCE_DIR")
     fs = make_fpga_slice(args.reference)
     np.savez_compressed(os.path.join(HERE, "fpga_slice.npz"), **fs)
     with open(os.path.join(HERE, "fpga_slice_sha256.json"), "w") as f:

@@ -9,7 +9,7 @@ import torch
 
 from llama3_8b_attention_optimize_b200 import kernels
 from oracle import golden as g
-from tests._util import bf16_ulp_of, bf16_words, randn_bf16
+from tests._util import bf16_ulp_of, bf16_words, randn_bf16, report_ulps, ulp_histogram
 
 pytestmark = pytest.mark.gpu
 
@@ -26,10 +26,12 @@ def _reference(q, kc, vc, lens, batches, heads):
 
 
 def _check(out, ref, batches, heads):
-    got = g.bf16_words_to_f32(bf16_words(out)[batches, heads])
+    sel = bf16_words(out)[batches, heads]
+    got = g.bf16_words_to_f32(sel)
     err = np.abs(got - ref)
     assert np.all(err <= np.maximum(1e-2, bf16_ulp_of(ref))), err.max()
     assert err.mean() <= 1e-3, err.mean()
+    return ulp_histogram(sel, g.to_bf16_words(ref))
 
 
 @pytest.mark.parametrize("B,Lmax,split", [(3, 100, 0), (2, 1000, 64), (4, 3000, 256), (2, 130, 128)])
@@ -94,7 +96,7 @@ def test_decode_c5_config_sampled():
     rng = np.random.default_rng(2)
     bs = rng.integers(0, B, 48)
     hs = rng.integers(0, Hq, 48)
-    _check(out, _reference(q, kc, vc, lens_np, bs, hs), bs, hs)
+    report_ulps("decode_c5_sampled_rows", _check(out, _reference(q, kc, vc, lens_np, bs, hs), bs, hs))
     # split length does not change the result beyond rounding
     out2 = kernels.decode(q, kc, vc, lens, split_len=4096)
     d = (out.float() - out2.float()).abs()

@@ -17,7 +17,7 @@ import torch
 
 from llama3_8b_attention_optimize_b200 import golden_model, kernels
 from oracle import golden as g
-from tests._util import bf16_ulp_of, bf16_words, randn_bf16, ulp_histogram, words_to_bf16
+from tests._util import bf16_ulp_of, bf16_words, randn_bf16, report_ulps, ulp_histogram, words_to_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -46,7 +46,7 @@ def _reshape(e: np.ndarray, *shape, axes=None) -> np.ndarray:
     return out
 
 
-def _check_bf16(got: torch.Tensor, exact: np.ndarray, min_exact: float = 0.97):
+def _check_bf16(got: torch.Tensor, exact: np.ndarray, min_exact: float = 0.97) -> dict:
     gw = bf16_words(got).reshape(exact.shape)
     ex = np.asarray(exact, dtype=np.float64)
     ew = g.to_bf16_words(ex.astype(np.float32))
@@ -55,6 +55,7 @@ def _check_bf16(got: torch.Tensor, exact: np.ndarray, min_exact: float = 0.97):
     allow = bf16_ulp_of(ex) * 1.0001 + 2.0 ** -20 * exact.absdot
     assert np.all(err <= allow), (err - allow).max()
     assert np.mean(gw == ew) >= min_exact, np.mean(gw == ew)
+    return ulp_histogram(gw, ew)
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 72), (257, 384, 520), (1024, 1024, 4096)])
@@ -168,7 +169,8 @@ def test_full_layer_matches_reference_dump():
             assert np.all(aerr <= np.maximum(1e-2, bf16_ulp_of(exact_attn))) and aerr.mean() <= 1e-3
             flat = attn.to(torch.bfloat16).transpose(0, 1).contiguous().view(S, -1)
             fe = _exact(flat, wo)
-            _check_bf16(dump["final_output"].to(torch.bfloat16), fe)
+            report_ulps("layer_s32_final_output_vs_float64_o_proj",
+                        _check_bf16(dump["final_output"].to(torch.bfloat16), fe))
             # against the reference's staged result: both approximate the exact layer, and
             # the fused path is the closer of the two
             Hq, S = fx["q_after_rope"].shape[:2]
@@ -204,7 +206,7 @@ def test_c4_projection_shapes_sampled_rows():
     for t, w, H in ((q, wq, 32), (k, wk, 8), (v, wv, 8)):
         _check_bf16(t[:, rows].transpose(0, 1), _reshape(_exact(h, w, rows), len(rows), H, 128))
     flat = attn.transpose(0, 1).contiguous().view(S, 4096)
-    _check_bf16(o[rows], _exact(flat, wo, rows))
+    report_ulps("c4_o_proj_sampled_rows_vs_float64", _check_bf16(o[rows], _exact(flat, wo, rows)))
 
 
 def test_layer_session_matches_facade_and_shards_sum():

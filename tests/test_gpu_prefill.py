@@ -15,7 +15,7 @@ import torch
 
 from llama3_8b_attention_optimize_b200 import kernels
 from oracle import golden as g
-from tests._util import bf16_ulp_of, bf16_words, randn_bf16, ulp_histogram, words_to_bf16
+from tests._util import bf16_ulp_of, bf16_words, randn_bf16, report_ulps as _report, ulp_histogram, words_to_bf16
 
 pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -84,7 +84,8 @@ def test_c1_config_all_rows_vs_oracle():
     out = kernels.prefill(q, k, v, cos, sin, rope_q=True, rope_k=True)
     kernels.device_check()
     qr, kr, vw = _rotated_words(q, S), _rotated_words(k, S), bf16_words(v)
-    mx, mean, _ = _check_rows(out, qr, kr, vw, [_all_rows(Hq, S)], tag="C1")
+    mx, mean, ulps = _check_rows(out, qr, kr, vw, [_all_rows(Hq, S)], tag="C1")
+    _report("prefill_c1_all_rows", ulps)
     # and against the bf16-staged golden pipeline (oracle restatement of run_full_attention)
     # The golden's bf16-staged pipeline rounds scores (|s| up to ~5 here) and weights to
     # bf16, which moves it up to ~1.6e-2 from the exact result; the kernel is held to
@@ -168,7 +169,23 @@ def test_c3_config_sampled_rows_and_properties():
         heads = rng.integers(0, Hq, 96)
         pos = np.concatenate([[0, 1, 127, 128, S - 1], rng.integers(0, S, 91)])
         rows.append((heads, pos))
-    _check_rows(out, _rotated_words(q, S), _rotated_words(k, S), bf16_words(v), rows, tag="C3")
+    qr, kr, vw = _rotated_words(q, S), _rotated_words(k, S), bf16_words(v)
+    _, _, ulps = _check_rows(out, qr, kr, vw, rows, tag="C3")
+    _report("prefill_c3_fused_sampled_rows", ulps)
+
+    # the benchmark's timed mode: K rotated by its own launch, Q inside the fused kernel
+    # (PrefillSession.run_device, rope="prepass_k"), checked against the oracle itself
+    from llama3_8b_attention_optimize_b200.session import PrefillSession
+    sess = PrefillSession(B, S, Hq, Hkv, rope="prepass_k")
+    sess.q.copy_(q)
+    sess.k.copy_(k)
+    sess.v.copy_(v)
+    bench_out = sess.run_device().clone()
+    kernels.device_check()
+    _, _, ulps = _check_rows(bench_out, qr, kr, vw, rows, tag="C3 prepass_k")
+    _report("prefill_c3_bench_mode_sampled_rows", ulps)
+    assert torch.equal(bench_out, out)
+    del sess, bench_out
 
     # KV-head shards computed separately are bit-identical to the full run
     sharded = torch.full_like(out, float("nan"))

@@ -61,13 +61,14 @@ def test_read_write_round_trip_and_format(tmp_path, fs):
     assert list(hexio.read_hex(q, 2)) == [0x00FF, 0x7FC0]
 
 
-@pytest.mark.parametrize("text,msg", [(b"12G4\n", "invalid HEX"), (b"1FFFF\n", "wider than BF16"),
-                                      (b"0001\n0002\n", "expected 3 words")])
+@pytest.mark.parametrize("text,msg", [(b"12G4\n", "line 1: '12G4' is not a 16-bit hex word"),
+                                      (b"0001\n\n1FFFF\n", "line 3: '1FFFF' is not a 16-bit hex word"),
+                                      (b"0001\n0002\n", "2 words, want 3")])
 def test_read_hex_rejects(tmp_path, text, msg):
     p = tmp_path / "bad.hex"
     p.write_bytes(text)
     with pytest.raises(ValueError, match=msg):
-        hexio.read_hex(p, 3 if msg.startswith("expected") else 1)
+        hexio.read_hex(p, 3 if msg.startswith("2 words") else 2)
     with pytest.raises(FileNotFoundError):
         hexio.read_hex(tmp_path / "missing.hex", 1)
 
@@ -77,24 +78,27 @@ def test_load_real_npy_checks(tmp_path, fs):
     p = tmp_path / "v.npy"
     np.save(p, good)
     assert np.array_equal(hexio.load_real_npy(p, (1, 128, 128)), good)
-    with pytest.raises(ValueError, match="expected shape"):
+    with pytest.raises(hexio.VectorFileError, match=r"shape \(1, 128, 128\), want \(4, 128, 128\)"):
         hexio.load_real_npy(p, (4, 128, 128))
     np.save(p, good.astype(np.float64))
-    with pytest.raises(TypeError):
+    with pytest.raises(hexio.VectorFileError, match="dtype float64, want float32"):
         hexio.load_real_npy(p, (1, 128, 128))
     bad = good.copy()
     bad[0, 0, 0] = np.nan
-    np.save(p, bad)
-    with pytest.raises(ValueError, match="NaN"):
-        hexio.load_real_npy(p, (1, 128, 128))
-    bad = good.copy()
     bad[0, 0, 1] = np.float32(1.0000001)
+    bad[0, 0, 2] = np.float32(1.0000001)
     np.save(p, bad)
-    with pytest.raises(ValueError, match="BF16"):
+    # every problem is reported in one error
+    with pytest.raises(hexio.VectorFileError, match="1 NaN/Inf words; 2 words that are not bf16"):
+        hexio.load_real_npy(p, (1, 128, 128))
+    np.save(p, bad[:, :64])
+    with pytest.raises(hexio.VectorFileError, match="shape .*; 1 NaN/Inf words; 2 words"):
         hexio.load_real_npy(p, (1, 128, 128))
     p.write_bytes(b"version https://git-lfs.github.com/spec/v1\noid sha256:00\nsize 1\n")
-    with pytest.raises(RuntimeError, match="LFS"):
+    with pytest.raises(hexio.VectorFileError, match="Git LFS placeholder"):
         hexio.load_real_npy(p, (1, 128, 128))
+    with pytest.raises(FileNotFoundError):
+        hexio.load_real_npy(tmp_path / "missing.npy", (1, 128, 128))
 
 
 def test_prepare_from_npy_and_existing_check(tmp_path, fs, sha):
@@ -112,5 +116,5 @@ def test_prepare_from_npy_and_existing_check(tmp_path, fs, sha):
     wrong.reshape(-1)[77] ^= 1
     ex = tmp_path / "existing.hex"
     hexio.write_hex(ex, wrong)
-    with pytest.raises(RuntimeError, match="at word 77"):
+    with pytest.raises(RuntimeError, match="1 of 65536 words differ .* first at word 77"):
         hexio.prepare_from_npy(gdir, tmp_path / "tb2", existing={"softmax_weights.npy": ex})

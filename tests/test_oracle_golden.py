@@ -83,16 +83,39 @@ def test_rope_tables_vs_reference_rom(fs):
 
 
 def test_rope_table_matches_torch_recipe():
+    """The oracle's (and the kernels') cos/sin tables against the golden's torch fp32
+    recipe (llama3_attention_golden_model.py:124-130) over 32769 positions, the longest
+    table the decode path builds.
+
+    The oracle rounds cos/sin of each fp32 angle, evaluated in double precision, to fp32
+    and then to bf16; torch evaluates them in fp32 with its own CPU math library.  The
+    two agree on every word except where torch's fp32 result sits on (or one fp32 ulp
+    from) the midpoint between two bf16 values, so that the fp32 evaluation decides the
+    bf16 rounding.  Over 32769 x 128 words this happens at one angle (position 27067,
+    pair 3: torch's fp32 sin is exactly -0.998046875, the midpoint, while the double
+    value lies just inside it), i.e. two words, each one bf16 ulp apart.  The test
+    requires exact agreement below position 8192 (every prefill configuration) and,
+    beyond it, that every difference is one ulp at such a midpoint.
+    """
     torch = pytest.importorskip("torch")
-    S, D, theta = 4096, 128, 500000.0
+    S, D, theta = 32769, 128, 500000.0
     inv = 1.0 / (theta ** (torch.arange(0, D, 2).float() / D))
     assert np.array_equal(inv.numpy(), g.inv_freq(D, theta))
     emb = torch.outer(torch.arange(S).float(), inv)
     emb = torch.cat([emb, emb], dim=-1)
-    ct = emb.cos().to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-    st = emb.sin().to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     cos, sin = g.rope_table(S, D, theta)
-    assert np.array_equal(cos, ct) and np.array_equal(sin, st)
+    n_diff = 0
+    for fn, ours in ((torch.cos, cos), (torch.sin, sin)):
+        f32 = fn(emb)
+        ref = f32.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        assert np.array_equal(ours[:8192], ref[:8192])
+        bad = np.argwhere(ours != ref)
+        n_diff += len(bad)
+        for i, j in bad:
+            assert _ulp(ours[i:i + 1, j], ref[i:i + 1, j]).max() == 1, (i, j)
+            low = int(f32[i, j].view(torch.int32).item()) & 0xFFFF  # fp32 bits below the bf16 word
+            assert abs(low - 0x8000) <= 1, (i, j, hex(low))
+    assert n_diff <= 8, n_diff
 
 
 def test_layer_fixture_all_stages_bit_exact(layer):
