@@ -7,10 +7,14 @@
 // TMEM, one round-to-nearest-even to bf16 at the end -- or an fp32 result, for the
 // row-parallel partial sums that are all-reduced across GPUs before that rounding.
 //
-// Persistent CTAs (one per SM) walk 128 x BN output tiles.  Warp roles:
-//   warp 0     TMA producer: A (128 x 64) and W (BN x 64) k-blocks into a ring
-//   warp 1     MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per k-block into one
-//              of two TMEM accumulators (the epilogue drains one while the next
+// Persistent CTAs (one per SM) walk 128 x BN output tiles, or persistent pairs of CTAs
+// (a cluster of two) walk 256 x BN tiles with tcgen05.mma.cta_group::2: each CTA loads
+// its 128 rows of A and half of W, the even CTA issues the MMAs, and every MMA commit
+// is sent to the barrier of each CTA of the pair.  Warp roles:
+//   warp 0     TMA producer: A (128 x 64) and W (BN x 64, pair: BN/2 x 64) k-blocks
+//              into a ring (pair: both CTAs' loads complete on the even CTA's barrier)
+//   warp 1     MMA issuer: 4 x tcgen05.mma (M=128 or 256, N=BN, K=16) per k-block into
+//              one of two TMEM accumulators (the epilogue drains one while the next
 //              tile accumulates into the other)
 //   warps 2-5  epilogue: tcgen05.ld -> bf16 (or fp32) -> swizzled staging -> TMA store
 //
@@ -26,8 +30,6 @@
 // weight tensor and output map, so the fused projection is a single launch.
 #include <cuda.h>
 
-#include <cstdlib>
-
 #include "common.cuh"
 #include "gqa_internal.h"
 
@@ -40,11 +42,16 @@ constexpr int kThreads = 192;
 constexpr int kMaxRegions = 3;
 constexpr int kMaxDest = 8;
 
-template <int BN>
+// kPair: a cluster of two CTAs computes one 256 x BN tile with tcgen05.mma.cta_group::2
+// (M = 256): each CTA holds its own 128 rows of A and half (BN / 2 rows) of W's k-block,
+// the even CTA issues the MMAs, and each CTA's TMEM receives its 128 rows of the result.
+template <int BN, bool kPair>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kWRows = kPair ? BN / 2 : BN;  // W rows this CTA loads per k-block
+  static constexpr int kTileM = kPair ? 2 * kBM : kBM;
+  static constexpr int kStages = kPair ? 6 : (BN == 256 ? 4 : 6);
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kWBytes = BN * kBK * 2;
+  static constexpr int kWBytes = kWRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kWBytes;
   static constexpr int kBoxBytes = kBM * 128;  // one 128-row x 128-byte store box
   static constexpr int kOffStaging = kStages * kStageBytes;
@@ -138,14 +145,81 @@ __device__ __forceinline__ const CUtensorMap* pick(const CUtensorMap* m0, const 
   return r == 0 ? m0 : (r == 1 ? m1 : m2);
 }
 
+// ---- CTA-pair helpers (cluster of two CTAs along x)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Arrive on an mbarrier (any CTA of the pair) once this thread's earlier pair MMAs are done.
+__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 4-D tiled load into this CTA's shared memory whose completion is counted on the
+// mbarrier at `bar_cluster` (the even CTA's barrier: the pair's loads share one count).
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* map, uint32_t bar_cluster, int c0, int c1,
+                                                 int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+template <bool kPair>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t dst_smem, uint32_t ncols) {
+  if (kPair)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+  else
+    tmem_alloc(dst_smem, ncols);
+}
+template <bool kPair>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if (kPair)
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  else
+    tmem_relinquish();
+}
+template <bool kPair>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if (kPair)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    tmem_dealloc(taddr, ncols);
+}
+
 // Byte offset of 16-byte unit j of row `row` in a 128-row x 128-byte SW128 box.
 __device__ __forceinline__ uint32_t box_unit(int row, int j) {
   return static_cast<uint32_t>(row * 128 + ((j ^ (row & 7)) << 4));
 }
 
-template <int BN>
+template <int BN, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, kPair>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(SITE_SMEM_ALIGN);
@@ -158,6 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   auto bar_acc_full = [&](int b) -> uint32_t { return sbase + C::kOffBar + 8 * (2 * C::kStages + b); };
   auto bar_acc_empty = [&](int b) -> uint32_t { return sbase + C::kOffBar + 8 * (2 * C::kStages + 2 + b); };
 
+  // Pair: rank 0 issues the MMAs; tiles are walked per cluster.
+  const uint32_t rank = kPair ? cluster_rank() : 0u;
+  const int unit = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int n_units = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar_full(s), 1);
@@ -165,13 +243,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_acc_full(b), 1);
-      mbar_init(bar_acc_empty(b), 128);
+      mbar_init(bar_acc_empty(b), kPair ? 256 : 128);  // pair: both CTAs' epilogue threads
     }
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(sbase + C::kOffTmemPtr, C::kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_g<kPair>(sbase + C::kOffTmemPtr, C::kTmemCols);
+    tmem_relinquish_g<kPair>();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&maps.a);
@@ -181,7 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if (kPair)
+    cluster_sync_all();  // both CTAs' barriers initialised before either signals the other
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::kOffTmemPtr);
 
@@ -190,37 +271,59 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (lane == 0) {
       bool ok = true;
       uint32_t it = 0;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
-        const int m0 = (tile % p.tiles_m) * kBM, n0 = (tile / p.tiles_m) * BN;
+      for (int tile = unit; ok && tile < p.n_tiles; tile += n_units) {
+        const int m0 = (tile % p.tiles_m) * C::kTileM + static_cast<int>(rank) * kBM;  // this CTA's rows
+        const int n0 = (tile / p.tiles_m) * BN;
         const int r = region_of(p, n0);
         const CUtensorMap* wm = pick(&maps.w[0], &maps.w[1], &maps.w[2], r);
-        const int b = m0 / p.S, s0 = m0 - b * p.S, wn = n0 - region_at(p, r).n0;
+        const int b = m0 / p.S, s0 = m0 - b * p.S;
+        const int wn = n0 - region_at(p, r).n0 + static_cast<int>(rank) * C::kWRows;
         for (int kb = 0; kb < p.n_kb; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t round = it / C::kStages;
           if (round > 0 && !(ok = mbar_wait(bar_empty(s), (round - 1) & 1u, SITE_PRODUCER))) break;
           const uint32_t dst = sbase + s * C::kStageBytes;
           const int k0 = kb * kBK;
-          mbar_expect_tx(bar_full(s), C::kStageBytes);
-          tma_load_4d(dst, &maps.a, bar_full(s), k0 % p.a_kin, s0, k0 / p.a_kin, b);
-          tma_load_4d(dst + C::kABytes, wm, bar_full(s), k0, wn, 0, 0);
+          if (kPair) {
+            // both CTAs' loads complete on the even CTA's barrier, which expects them all
+            const uint32_t full0 = map_to_rank(bar_full(s), 0);
+            if (rank == 0) mbar_expect_tx(bar_full(s), 2 * C::kStageBytes);
+            tma_load_4d_pair(dst, &maps.a, full0, k0 % p.a_kin, s0, k0 / p.a_kin, b);
+            tma_load_4d_pair(dst + C::kABytes, wm, full0, k0, wn, 0, 0);
+          } else {
+            mbar_expect_tx(bar_full(s), C::kStageBytes);
+            tma_load_4d(dst, &maps.a, bar_full(s), k0 % p.a_kin, s0, k0 / p.a_kin, b);
+            tma_load_4d(dst + C::kABytes, wm, bar_full(s), k0, wn, 0, 0);
+          }
         }
       }
-      // every issued load lands before the CTA exits
-      const uint32_t first = it > static_cast<uint32_t>(C::kStages) ? it - C::kStages : 0u;
-      for (uint32_t i = first; i < it; ++i)
-        mbar_wait(bar_full(static_cast<int>(i % C::kStages)), (i / C::kStages) & 1u, SITE_PRODUCER);
+      // every issued load lands before the CTA exits (pair: the even CTA's MMA waited for
+      // all of them, and both CTAs meet at the cluster barrier before exiting)
+      if (!kPair) {
+        const uint32_t first = it > static_cast<uint32_t>(C::kStages) ? it - C::kStages : 0u;
+        for (uint32_t i = first; i < it; ++i)
+          mbar_wait(bar_full(static_cast<int>(i % C::kStages)), (i / C::kStages) & 1u, SITE_PRODUCER);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kId = idesc_bf16_f32(kBM, BN, false);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t kId = idesc_bf16_f32(C::kTileM, BN, false);
       constexpr uint32_t kHi = sdesc_hi_sw128(1024);
       const uint32_t lo0 = sdesc_lo(sbase, 16);
+      // pair: a barrier in each CTA is told when the pair's MMAs are done
+      auto commit = [&](uint32_t bar) {
+        if (kPair) {
+          umma_commit_pair(map_to_rank(bar, 0));
+          umma_commit_pair(map_to_rank(bar, 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
       bool ok = true;
       uint32_t it = 0, t_iter = 0;
-      for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
+      for (int tile = unit; ok && tile < p.n_tiles; tile += n_units, ++t_iter) {
         const int ab = static_cast<int>(t_iter & 1u);
         const uint32_t use = t_iter >> 1;
         if (use > 0 && !(ok = mbar_wait_spin(bar_acc_empty(ab), (use - 1) & 1u, SITE_MMA))) break;
@@ -233,11 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           const uint32_t a_lo = lo0 + static_cast<uint32_t>(s * C::kStageBytes) / 16u;
           const uint32_t w_lo = a_lo + C::kABytes / 16u;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_ss_lohi(d, a_lo + 2u * kk, w_lo + 2u * kk, kHi, kId, (kb | kk) ? 1u : 0u);
-          umma_commit(bar_empty(s));
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            if (kPair)
+              umma_ss_pair(d, a_lo + 2u * kk, w_lo + 2u * kk, kHi, kId, (kb | kk) ? 1u : 0u);
+            else
+              umma_ss_lohi(d, a_lo + 2u * kk, w_lo + 2u * kk, kHi, kId, (kb | kk) ? 1u : 0u);
+          }
+          commit(bar_empty(s));
         }
-        if (ok) umma_commit(bar_acc_full(ab));
+        if (ok) commit(bar_acc_full(ab));
       }
     }
     __syncwarp();
@@ -252,8 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint8_t* const stg1_p = stg0_p + C::kBoxBytes;
     bool ok = true;
     uint32_t t_iter = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
-      const int m0 = (tile % p.tiles_m) * kBM, n0 = (tile / p.tiles_m) * BN;
+    for (int tile = unit; tile < p.n_tiles; tile += n_units, ++t_iter) {
+      const int m0 = (tile % p.tiles_m) * C::kTileM + static_cast<int>(rank) * kBM;  // this CTA's rows
+      const int n0 = (tile / p.tiles_m) * BN;
       const int r = region_of(p, n0);
       const Region rg = region_at(p, r);
       const CUtensorMap* cm = pick(&maps.c[0], &maps.c[1], &maps.c[2], r);
@@ -344,7 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
         if (cyc == n_cycles - 1) {  // accumulator fully read: the MMA may reuse it
           tc_fence_before();
-          mbar_arrive(bar_acc_empty(ab));
+          if (kPair)
+            mbar_arrive_cluster(map_to_rank(bar_acc_empty(ab), 0));
+          else
+            mbar_arrive(bar_acc_empty(ab));
         }
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
@@ -385,7 +496,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
   // ---- teardown
   tc_fence_before();
-  __syncthreads();
+  if (kPair)
+    cluster_sync_all();  // neither CTA leaves while the other may still signal it
+  else
+    __syncthreads();
   if (p.scatter_rows > 0 && threadIdx.x == 0) {
     // The last CTA to finish tells every destination that its rows are complete, unless
     // a wait of this grid gave up (a CTA that failed skipped its stores): then no flag is
@@ -404,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    tmem_dealloc_g<kPair>(tmem, C::kTmemCols);
   }
 }
 
@@ -435,9 +549,9 @@ struct Launch {
   uint32_t sig_epoch;
 };
 
-template <int BN>
+template <int BN, bool kPair>
 int launch_bn(const Launch& L, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, kPair>;
   Maps maps;
   int rc;
   const int box_a[4] = {kBK, kBM, 1, 1};
@@ -447,21 +561,21 @@ int launch_bn(const Launch& L, cudaStream_t stream) {
     const long long wd[4] = {L.K, L.reg[rr].n1 - L.reg[rr].n0, 1, 1};
     const long long ws[3] = {static_cast<long long>(L.ldw[rr]) * 2, static_cast<long long>(L.ldw[rr]) * 2 * wd[1],
                              static_cast<long long>(L.ldw[rr]) * 2 * wd[1]};
-    const int box_w[4] = {kBK, BN, 1, 1};
+    const int box_w[4] = {kBK, C::kWRows, 1, 1};
     if ((rc = make_tmap_4d(&maps.w[r], L.w[rr], 2, wd, ws, box_w)) != GQA_OK) return rc;
     const int box_c[4] = {L.out_f32 ? 32 : 64, kBM, 1, 1};
     if ((rc = make_tmap_4d(&maps.c[r], L.c[rr], L.out_f32 ? 4 : 2, L.c_dims[rr], L.c_strides[rr], box_c)) != GQA_OK)
       return rc;
   }
   static std::atomic<uint64_t> attr_done{0};
-  if ((rc = ensure_smem_attr(gemm_kernel<BN>, C::kSmemBytes, attr_done)) != GQA_OK) return rc;
+  if ((rc = ensure_smem_attr(gemm_kernel<BN, kPair>, C::kSmemBytes, attr_done)) != GQA_OK) return rc;
   Params p;
   p.M = L.M;
   p.N = L.N;
   p.K = L.K;
   p.S = L.S;
   p.a_kin = L.a_kin;
-  p.tiles_m = (L.M + kBM - 1) / kBM;
+  p.tiles_m = (L.M + C::kTileM - 1) / C::kTileM;
   p.tiles_n = (L.N + BN - 1) / BN;
   p.n_tiles = p.tiles_m * p.tiles_n;
   p.n_kb = (L.K + kBK - 1) / kBK;
@@ -483,8 +597,35 @@ int launch_bn(const Launch& L, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int cap = L.max_ctas > 0 && L.max_ctas < sms ? L.max_ctas : sms;
-  const int grid = p.n_tiles < cap ? p.n_tiles : cap;
-  gemm_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(maps, p);
+  if (!kPair) {
+    const int grid = p.n_tiles < cap ? p.n_tiles : cap;
+    gemm_kernel<BN, false><<<grid, kThreads, C::kSmemBytes, stream>>>(maps, p);
+    return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+  }
+  // one cluster of two CTAs per tile slot; at most as many clusters as fit at once
+  static std::atomic<int> max_clusters{0};
+  int mc = max_clusters.load(std::memory_order_acquire);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (mc == 0) {
+    cfg.gridDim = dim3(sms & ~1);
+    if (cudaOccupancyMaxActiveClusters(&mc, gemm_kernel<BN, true>, &cfg) != cudaSuccess || mc <= 0) return GQA_ERR_CUDA;
+    max_clusters.store(mc, std::memory_order_release);
+  }
+  int clusters = cap / 2 < mc ? cap / 2 : mc;
+  if (clusters > p.n_tiles) clusters = p.n_tiles;
+  if (clusters < 1) clusters = 1;
+  cfg.gridDim = dim3(2 * clusters);
+  if (cudaLaunchKernelEx(&cfg, gemm_kernel<BN, true>, maps, p) != cudaSuccess) return GQA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 
@@ -503,31 +644,19 @@ int pick_bn(const Launch& L, int sms) {
   return t128 <= sms ? 128 : 256;
 }
 
-// GQA_GEMM_BN=128|256 overrides the tile width (for measurements); region
-// boundaries that are not multiples of 256 always use 128.
-int forced_bn() {
-  static const int bn = [] {
-    const char* e = getenv("GQA_GEMM_BN");
-    return e ? atoi(e) : 0;
-  }();
-  return bn;
-}
-
 int launch(const Launch& L, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int bn = pick_bn(L, sms);
-  if (forced_bn() == 128 || (forced_bn() == 256 && bn == 256)) bn = forced_bn();
-  if (forced_bn() == 256 && bn == 128) {
-    bool ok256 = true;
-    for (int r = 1; r < L.n_regions; ++r) ok256 = ok256 && L.reg[r].n0 % 256 == 0;
-    if (L.out_f32 == 0)
-      for (int r = 0; r < L.n_regions; ++r)
-        ok256 = ok256 && !(L.reg[r].head_major && (L.reg[r].n1 - L.reg[r].n0) % 256);
-    if (ok256) bn = 256;
-  }
-  return bn == 256 ? launch_bn<256>(L, stream) : launch_bn<128>(L, stream);
+  const int bn = pick_bn(L, sms);
+  // CTA pairs (256-row tiles, W rows split between the two CTAs) wherever the rows
+  // divide into pair tiles; the scatter epilogue keeps single CTAs.  Pairs compute the
+  // same sums in the same order (bit-identical results) with half of W per CTA: 1.28
+  // against 1.23 PFLOP/s at 4096^3 (bf16 out), the rest of the gap to cuBLAS being the
+  // 3.46 waves of 256 x 256 tiles on 74 pairs and the power cap.
+  const bool pair = L.scatter_rows == 0 && L.M % (2 * kBM) == 0;
+  if (pair) return bn == 256 ? launch_bn<256, true>(L, stream) : launch_bn<128, true>(L, stream);
+  return bn == 256 ? launch_bn<256, false>(L, stream) : launch_bn<128, false>(L, stream);
 }
 
 }  // namespace gemm

@@ -257,3 +257,29 @@ def test_o_proj_rows_chunks_equal_full_call():
     kernels.device_check()
     assert torch.all(part[:256] == 5.0) and torch.all(part[384:] == 5.0)
     assert torch.equal(part[256:384], kernels.o_proj(attn, wo, out_f32=True)[256:384])
+
+
+def test_cta_pair_tiles_equal_single_cta_tiles():
+    """Row counts that divide into 256-row tiles run on CTA pairs (tcgen05.mma.cta_group::2,
+    half of W per CTA); other row counts run on single CTAs.  Both accumulate the same
+    products in the same order, so every row of a pair-tiled call equals the same row of
+    single-CTA calls bit for bit (bf16 and fp32 outputs, with and without a grid cap)."""
+    g0 = torch.Generator(device="cuda").manual_seed(78)
+    Hq, S, N = 8, 1024, 4096
+    attn = (torch.randn(Hq, S, 128, generator=g0, device="cuda")).to(torch.bfloat16)
+    wo = (torch.randn(N, 4096, generator=g0, device="cuda") * 0.02).to(torch.bfloat16)
+    for f32 in (True, False):
+        full = kernels.o_proj(attn, wo, head_begin=1, out_f32=f32)  # 1024 rows: CTA pairs
+        dt = torch.float32 if f32 else torch.bfloat16
+        got = torch.full((S, N), float("nan"), dtype=dt, device="cuda")
+        # chunks of 128 and 384 rows run on single CTAs, the 256-row chunk on a pair
+        for (s0, n), cap in zip([(0, 128), (128, 384), (512, 256), (768, 128), (896, 128)], (0, 0, 10, 0, 5)):
+            kernels.o_proj_rows(attn, wo, got, s0, n, head_begin=1, out_f32=f32, max_ctas=cap)
+        kernels.device_check()
+        assert torch.equal(got, full)
+    x = (torch.randn(768, 4096, generator=g0, device="cuda")).to(torch.bfloat16)
+    w = (torch.randn(512, 4096, generator=g0, device="cuda") * 0.02).to(torch.bfloat16)
+    pair = kernels.linear(x, w)                                   # 768 rows: pairs
+    single = torch.cat([kernels.linear(x[i:i + 128], w) for i in range(0, 768, 128)])  # 128 rows each
+    kernels.device_check()
+    assert torch.equal(pair, single)
