@@ -33,9 +33,18 @@ def ulp_dist(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 
 
 def ulp_histogram(a_words: np.ndarray, b_words: np.ndarray) -> dict:
+    """Share of elements whose bf16 words are 0, 1, 2 or more ulps apart, over all
+    elements and ("big_*") over those whose reference value b has |b| >= 1/4 (below that
+    a tiny absolute error spans many ulps, and outputs near zero dominate the counts)."""
     d = ulp_dist(a_words, b_words)
-    return {"0": float((d == 0).mean()), "1": float((d == 1).mean()), "2": float((d == 2).mean()),
-            ">2": float((d > 2).mean()), "max": int(d.max()) if d.size else 0}
+    mag = np.abs((np.asarray(b_words, np.uint32) << 16).view(np.float32))
+    big = d[mag >= 0.25]
+    frac = lambda x, sel: float(sel.mean()) if x.size else 0.0  # noqa: E731
+    return {"0": frac(d, d == 0), "1": frac(d, d == 1), "2": frac(d, d == 2), ">2": frac(d, d > 2),
+            "max": int(d.max()) if d.size else 0,
+            "big_share": float(big.size / d.size) if d.size else 0.0,
+            "big_0": frac(big, big == 0), "big_1": frac(big, big == 1), "big_>1": frac(big, big > 1),
+            "big_max": int(big.max()) if big.size else 0}
 
 
 def rows_reference(q_rot_w, k_rot_w, v_w, heads, pos, causal=True, n_keys=None) -> np.ndarray:
@@ -55,8 +64,10 @@ def report_ulps(name: str, hists) -> dict:
     value) under `name` and, when GQA_PARITY_REPORT names a file, append it there as a
     JSON line.  `hists` is one ulp_histogram dict or a list of them (equal weights)."""
     hists = [hists] if isinstance(hists, dict) else list(hists)
-    hist = {k: sum(h[k] for h in hists) / len(hists) for k in ("0", "1", "2", ">2")}
+    keys = ("0", "1", "2", ">2", "big_share", "big_0", "big_1", "big_>1")
+    hist = {k: sum(h[k] for h in hists) / len(hists) for k in keys}
     hist["max"] = max(h["max"] for h in hists)
+    hist["big_max"] = max(h["big_max"] for h in hists)
     print(f"ulp histogram {name}: {hist}")
     path = os.environ.get("GQA_PARITY_REPORT")
     if path:
