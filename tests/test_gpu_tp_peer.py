@@ -3,9 +3,11 @@
 * gqa_tp_reduce_gather_bf16 (pull) and gqa_tp_o_proj_exchange_bf16 (fused push) give the
   same layer output, step after step, at 2, 4 and 8 ranks (each size skipped when the box
   has fewer GPUs): bit-identical to the NCCL all-reduce path at 2 ranks (an fp32 sum of
-  two terms does not depend on the order), and within one bf16 ulp of the correctly
-  rounded float64 sum of all ranks' partials at every size (NCCL's summation order is
-  unspecified, so above 2 ranks the paths may differ from it by one rounding).
+  two terms does not depend on the order), and at every size within one bf16 ulp of the
+  float64 sum of all ranks' partials plus the fp32 summation error (world - 1 additions
+  at 2^-24 of the partials' magnitudes: where the partials cancel, an fp32 sum is more
+  than one bf16 ulp from the exact value, for NCCL's order too); NCCL is held to the same
+  bound, and the ulp histogram of the exchange against the exact sum is printed.
 * A peer that never signals -- a missing buffer on one GPU, or a rank that skips a step --
   ends the waits with GQA_ERR_DEVICE_TIMEOUT instead of a hang, on the pull and the fused
   path, and the GPU stays usable.
@@ -82,16 +84,25 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
             # the correctly rounded sum of every rank's partial
             parts = [torch.empty_like(part) for _ in range(world)]
             dist.all_gather(parts, part)
-            exact = torch.stack(parts).double().sum(0).float().to(torch.bfloat16)
+            stack = torch.stack(parts).double()
+            exact64 = stack.sum(0)
+            exact = exact64.float().to(torch.bfloat16)
+            # one bf16 rounding of an fp32 sum: within one bf16 ulp of the exact sum plus the
+            # fp32 summation error (world - 1 additions, 2^-24 of the running magnitudes each)
+            ulp = torch.exp2(torch.floor(torch.log2(exact64.abs().clamp_min(2.0 ** -126))) - 7)
+            allow = ulp + (world - 1) * 2.0 ** -24 * stack.abs().sum(0)
             assert torch.equal(b, c), (rank, step, (b.float() - c.float()).abs().max().item())
             for got, hh in ((c, hist), (a, nccl_hist)):
                 d = (_ulp_key(got) - _ulp_key(exact)).abs()
                 hh["0"] += int((d == 0).sum())
                 hh["1"] += int((d == 1).sum())
                 hh[">1"] += int((d > 1).sum())
+                err = (got.double() - exact64).abs()
+                assert bool((err <= allow).all()), (rank, step, float((err - allow).max()))
             if world == 2:
                 assert torch.equal(a, b), (rank, step, (a.float() - b.float()).abs().max().item())
-        assert hist[">1"] == 0 and nccl_hist[">1"] == 0, (hist, nccl_hist)
+        # more than one ulp only where the partials cancel: a small share of the outputs
+        assert hist[">1"] <= 1e-4 * sum(hist.values()), hist
         p2p.close()
         fused.close()
         with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
@@ -109,7 +120,8 @@ def test_peer_reduction_equals_all_reduce(tmp_path, world):
     hists = [json.loads((tmp_path / f"rank{r}.json").read_text()) for r in range(world)]
     total = {k: sum(h["peer_vs_exact"][k] for h in hists) for k in ("0", "1", ">1")}
     n = sum(total.values())
-    print(f"world {world}: peer exchange vs float64 sum: 0 ulp {total['0'] / n:.6f}, 1 ulp {total['1'] / n:.6f}")
+    print(f"world {world}: peer exchange vs float64 sum: 0 ulp {total['0'] / n:.6f}, 1 ulp {total['1'] / n:.6f}, "
+          f"more {total['>1'] / n:.2e}")
 
 
 def _skip_worker(rank: int, world: int, port: int, out_dir: str):
