@@ -265,6 +265,9 @@ class FullLayerSession:
         if self.reduce in ("p2p", "p2p_fused"):
             if B != 1:
                 raise ValueError("reduce='p2p' takes one sequence")
+            if self.reduce == "p2p_fused" and ((S // world) % 128 or hidden % 256):
+                raise ValueError("reduce='p2p_fused' needs S / world to be a multiple of 128 rows and hidden a "
+                                 "multiple of 256 (the o_proj tiles each rank stores into its owners)")
             self.peer = PeerExchange(S, hidden, rank, world, group, self.device)
             self.partial, self.out = self.peer.partial.view(B, S, hidden), self.peer.out.view(B, S, hidden)
         self._mine = (mk(B * S // world, hidden, dt=torch.float32) if self.reduce == "rs_ag" else None)

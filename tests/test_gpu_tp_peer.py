@@ -63,7 +63,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
     from llama3_8b_attention_optimize_b200.layer import FullLayerSession
 
     try:
-        S = 512
+        S = 1024  # the fused exchange needs S / world to be a multiple of 128 rows
         g, (wq, wk, wv, wo) = _weights(dev)
         ref = FullLayerSession(S, rank=rank, world=world, device=dev)
         p2p = FullLayerSession(S, rank=rank, world=world, device=dev, reduce="p2p")
