@@ -31,8 +31,12 @@
 //              their partial row max through shared memory)
 //   warp 16    TMA producer (Q tiles of each unit, then K0 K1 V0 K2 V1 ... into a
 //              3-stage ring)
-//   warp 17    tcgen05.mma issuer (one elected thread) + TMEM allocator
-//   warps 18-19 RoPE of K tiles in shared memory (FLAG_ROPE_K); Q tiles are rotated
+//   warps 17-18 tcgen05.mma issuers, one per Q tile (lane 0 issues QK_t and PV_t);
+//              warp 17 also allocates TMEM.  A single thread can start a 128x128x16
+//              MMA only every ~85-90 cycles against 64 cycles of tensor work (measured
+//              on B200), so one issuer would cap the tensor pipe near 70 %; two issue
+//              streams interleave and keep it fed.
+//   warp 19    RoPE of K tiles in shared memory (FLAG_ROPE_K); Q tiles are rotated
 //              by the softmax threads (FLAG_ROPE_Q), the next unit's before the
 //              current unit's epilogue
 // TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
@@ -63,8 +67,9 @@ constexpr int kHalf = kTileBytes / 2;         // one 64-column swizzle block of 
 constexpr int kSoftmaxThreads = 512;  // warps 0-15
 constexpr float kRescaleLog2 = 16.0f;
 constexpr int kWarpProducer = 16;
-constexpr int kWarpMma = 17;
-constexpr int kWarpRope0 = 18;
+constexpr int kWarpMma = 17;   // issues the MMAs of Q tile 0
+constexpr int kWarpMma1 = 18;  // issues the MMAs of Q tile 1
+constexpr int kWarpRope0 = 19;
 constexpr int kThreads = 640;
 // Register split (setmaxnreg): the launch gives every thread kRegsLaunch registers; the
 // helper warpgroup (warps 16-19) gives some back and the four softmax warpgroups take
@@ -90,33 +95,23 @@ static_assert(kSmemBytes <= 232448, "shared memory over the per-block limit");
 enum : int {
   B_QFULL = 0,     // [2]  TMA Q tile t of the current unit landed
   B_QREADY = 2,    // [2]  Q tile t (rotated) visible to the tensor core, 256 arrivals
-  B_QEMPTY = 4,    // [1]  last QK^T of the unit complete: the Q tiles may be reloaded
+  B_QEMPTY = 4,    // [1]  last QK^T of both tiles complete (one arrival per issuer)
   B_KVFULL = 5,    // [3]  TMA K/V stage landed
-  B_KVEMPTY = 8,   // [3]  MMAs reading the stage completed
-  B_KREADY = 11,   // [4]  K tile rotated (slot k % 4), 64 arrivals
+  B_KVEMPTY = 8,   // [3]  MMAs reading the stage completed (one arrival per issuer)
+  B_KREADY = 11,   // [4]  K tile rotated (slot k % 4), 32 arrivals
   B_SFULL = 15,    // [2]  S_t = Q_t K^T complete
-  B_SFREE = 17,    // [2]  S_t copied to registers (kMmaOrder 0: one barrier for both tiles)
-  B_PREADY = 19,   // [2]  P_t in shared memory, O_t rescaled (kMmaOrder 0: one for both)
+  B_SFREE = 17,    // [2]  S_t copied to registers
+  B_PREADY = 19,   // [2]  P_t in shared memory, O_t rescaled
   B_PVDONE = 21,   // [2]  O_t += P_t V complete (P_t buffer free)
-  B_DRAIN = 23,    // [1]  every MMA of the CTA complete
+  B_DRAIN = 23,    // [2]  every MMA of issuer t complete
 };
-// Order of the tensor-core work per K tile j:
-//   0: QK0(j+1) QK1(j+1) PV0(j) PV1(j), S/P hand-offs joint for both tiles
-//   1: same order, hand-offs per tile
-//   2: QK0(j+1) PV0(j) QK1(j+1) PV1(j), hand-offs per tile (the tiles' softmax phases
-//      half an iteration apart)
-constexpr int kMmaOrder = 1;
-// One mbarrier arrival per softmax warp (after __syncwarp) instead of one per thread
-// (measured no faster here; the per-thread arrivals are kept).
-constexpr bool kWarpArrive = false;
-constexpr int kArriveDiv = kWarpArrive ? 32 : 1;
-constexpr int kHandoffThreads = kMmaOrder == 0 ? kSoftmaxThreads : kSoftmaxThreads / 2;
+constexpr int kHandoffThreads = kSoftmaxThreads / 2;  // per-tile hand-offs: one tile's 256 threads
 // Exponentials of unmasked chunks partly on the FMA pipe (a cubic fit of 2^f, a quarter
 // of the pairs): with the bf16-consistent row sums below the kernel is MUFU-bound enough
 // for this to pay (about 10 % measured).
 constexpr bool kEmulateExp = true;
-__device__ __forceinline__ int sfree_bar(int t) { return B_SFREE + (kMmaOrder == 0 ? 0 : t); }
-__device__ __forceinline__ int pready_bar(int t) { return B_PREADY + (kMmaOrder == 0 ? 0 : t); }
+__device__ __forceinline__ int sfree_bar(int t) { return B_SFREE + t; }
+__device__ __forceinline__ int pready_bar(int t) { return B_PREADY + t; }
 constexpr int kKReadySlots = 4;
 
 enum : int {  // error sites reported through g_gqa_dev_error
@@ -188,15 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
-  // softmax hand-off: the whole warp (converged) arrives once, or each thread does
-  auto warp_arrive = [&](uint32_t b) {
-    if (kWarpArrive) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(b);
-    } else {
-      mbar_arrive(b);
-    }
-  };
+  // softmax hand-off: every thread arrives (one arrival per warp after __syncwarp
+  // measured no faster)
+  auto warp_arrive = [&](uint32_t b) { mbar_arrive(b); };
 
   const bool causal = (p.flags & GQA_FLAG_CAUSAL) != 0;
   const bool rope_q = (p.flags & GQA_FLAG_ROPE_Q) != 0;
@@ -227,21 +216,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B_QFULL + t), 1);
-      mbar_init(bar(B_QREADY + t), 256 / kArriveDiv);
+      mbar_init(bar(B_QREADY + t), 256);
       mbar_init(bar(B_SFULL + t), 1);
       mbar_init(bar(B_PVDONE + t), 1);
     }
-    mbar_init(bar(B_QEMPTY), 1);
+    mbar_init(bar(B_QEMPTY), 2);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(B_KVFULL + s), 1);
-      mbar_init(bar(B_KVEMPTY + s), 1);
+      mbar_init(bar(B_KVEMPTY + s), 2);
     }
-    for (int k = 0; k < kKReadySlots; ++k) mbar_init(bar(B_KREADY + k), 64);
+    for (int k = 0; k < kKReadySlots; ++k) mbar_init(bar(B_KREADY + k), 32);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(B_SFREE + t), kHandoffThreads / kArriveDiv);
-      mbar_init(bar(B_PREADY + t), kHandoffThreads / kArriveDiv);
+      mbar_init(bar(B_SFREE + t), kHandoffThreads);
+      mbar_init(bar(B_PREADY + t), kHandoffThreads);
     }
     mbar_init(bar(B_DRAIN), 1);
+    mbar_init(bar(B_DRAIN + 1), 1);
     fence_mbar_init();
   }
   if (warp == kWarpMma) {
@@ -314,40 +304,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kWarpMma || warp == kWarpMma1) {
+    // ------------------------------------------------------------ MMA issuers
+    // One issuing thread can start a 128x128x16 tcgen05.mma only every ~85 cycles, a
+    // third slower than the tensor core runs it, so each Q tile has its own issuer: warp
+    // kWarpMma + t issues QK_t and PV_t, and the two streams interleave in the pipe.
     regs_dec<kRegsHelper>();
+    const int tq = warp - kWarpMma;  // Q tile of this issuer
     if (lane == 0) {
       constexpr uint32_t kIdQK = idesc_bf16_f32(128, kBN, false);
       constexpr uint32_t kIdPV = idesc_bf16_f32(128, kD, true);
-      // Descriptor halves computed once; each MMA adds a compile-time offset (in
-      // 16-byte units) to the low word.  K-major operands (Q, K, P): LBO unused;
-      // V is MN-major with its two 64-dim blocks kHalf apart (LBO = kHalf).
       constexpr uint32_t kHi = sdesc_hi_sw128(1024);
-      const uint32_t q_lo = sdesc_lo(sbase + kOffQ, 16);
-      const uint32_t p_lo = sdesc_lo(sbase + kOffP, 16);
+      const uint32_t q_lo = sdesc_lo(sbase + kOffQ + tq * kTileBytes, 16);
+      const uint32_t p_lo = sdesc_lo(sbase + kOffP + tq * kTileBytes, 16);
       const uint32_t kv_lo = sdesc_lo(sbase + kOffKV, 16);
       const uint32_t v_lo = sdesc_lo(sbase + kOffKV, kHalf);
       constexpr uint32_t kTile16 = kTileBytes / 16;
+      const uint32_t dS = tmem + colS(tq), dO = tmem + colO(tq);
       // S_t = Q_t K^T over d = 128 (8 k-steps of 16; both operands K-major SW128)
-      auto issue_qk = [&](int t, int s) {
-        const uint32_t a0 = q_lo + t * kTile16, b0 = kv_lo + s * kTile16;
-        const uint32_t d = tmem + colS(t);
+      auto issue_qk = [&](int s) {
+        const uint32_t b0 = kv_lo + s * kTile16;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = ((kk >> 2) * kHalf + (kk & 3) * 32) / 16;
-          umma_ss_lohi(d, a0 + off, b0 + off, kHi, kIdQK, kk > 0 ? 1u : 0u);
+          umma_ss_lohi(dS, q_lo + off, b0 + off, kHi, kIdQK, kk > 0 ? 1u : 0u);
         }
       };
       // O_t (+)= P_t V over 128 keys (8 k-steps; P K-major SW128, V MN-major SW128)
-      auto issue_pv = [&](int t, int s, uint32_t acc) {
-        const uint32_t a0 = p_lo + t * kTile16, b0 = v_lo + s * kTile16;
-        const uint32_t d = tmem + colO(t);
-        umma_ss_lohi(d, a0, b0, kHi, kIdPV, acc);
+      auto issue_pv = [&](int s, uint32_t acc) {
+        const uint32_t b0 = v_lo + s * kTile16;
+        umma_ss_lohi(dO, p_lo, b0, kHi, kIdPV, acc);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk) {
           const uint32_t off = ((kk >> 2) * kHalf + (kk & 3) * 32) / 16;
-          umma_ss_lohi(d, a0 + off, b0 + kk * (2048 / 16), kHi, kIdPV, 1u);
+          umma_ss_lohi(dO, p_lo + off, b0 + kk * (2048 / 16), kHi, kIdPV, 1u);
         }
       };
       bool ok = true;
@@ -365,89 +355,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ii = L + load_idx_k(j);
           return mbar_wait_spin(bar(B_KVFULL + ii % kStages), (ii / kStages) & 1u, SITE_MMA);
         };
-        // Q of this unit ready, and the S buffers released by the previous unit's softmax
-        ok = mbar_wait_spin(bar(B_QREADY + 0), uc & 1, SITE_MMA) && mbar_wait_spin(bar(B_QREADY + 1), uc & 1, SITE_MMA);
-        ok = ok && wait_k(0) &&
-             (Gb == 0 || (mbar_wait_spin(bar(sfree_bar(0)), (Gb - 1) & 1u, SITE_MMA) &&
-                          mbar_wait_spin(bar(sfree_bar(1)), (Gb - 1) & 1u, SITE_MMA)));
+        // Q tile of this unit ready, and S_t released by the previous unit's softmax
+        ok = mbar_wait_spin(bar(B_QREADY + tq), uc & 1, SITE_MMA) && wait_k(0) &&
+             (Gb == 0 || mbar_wait_spin(bar(sfree_bar(tq)), (Gb - 1) & 1u, SITE_MMA));
         if (!ok) break;
         {
           const int sk = static_cast<int>((L + load_idx_k(0)) % kStages);
           tc_fence_after();
-          issue_qk(0, sk);
-          umma_commit(bar(B_SFULL + 0));
-          issue_qk(1, sk);
-          umma_commit(bar(B_SFULL + 1));
+          issue_qk(sk);
+          umma_commit(bar(B_SFULL + tq));
           umma_commit(bar(B_KVEMPTY + sk));
           if (n == 1) umma_commit(bar(B_QEMPTY));
         }
         for (int j = 0; ok && j < n; ++j) {
           const uint32_t g = Gb + j;
-          const int sk = static_cast<int>((L + load_idx_k(j + 1)) % kStages);  // used when j + 1 < n
           const uint32_t iv = L + load_idx_v(j, n);
           const int sv = static_cast<int>(iv % kStages);
-          if (kMmaOrder == 2) {
-            // QK0(j+1) PV0(j) QK1(j+1) PV1(j)
-            if (j + 1 < n) {
-              ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(0)), g & 1u, SITE_MMA);
-              if (!ok) break;
-              tc_fence_after();
-              issue_qk(0, sk);
-              umma_commit(bar(B_SFULL + 0));
-            }
-            ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
-                 mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(0, sv, j > 0 ? 1u : 0u);
-            umma_commit(bar(B_PVDONE + 0));
-            if (j + 1 < n) {
-              ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
-              if (!ok) break;
-              tc_fence_after();
-              issue_qk(1, sk);
-              umma_commit(bar(B_SFULL + 1));
-              umma_commit(bar(B_KVEMPTY + sk));
-              if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
-            }
-            ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(1, sv, j > 0 ? 1u : 0u);
-            umma_commit(bar(B_PVDONE + 1));
-            umma_commit(bar(B_KVEMPTY + sv));
-            continue;
-          }
           if (j + 1 < n) {
-            // next S as soon as the softmax warps hold S(j) in registers
-            ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(0)), g & 1u, SITE_MMA);
+            // next S as soon as this tile's softmax holds S(j) in registers
+            const int sk = static_cast<int>((L + load_idx_k(j + 1)) % kStages);
+            ok = wait_k(j + 1) && mbar_wait_spin(bar(sfree_bar(tq)), g & 1u, SITE_MMA);
             if (!ok) break;
             tc_fence_after();
-            issue_qk(0, sk);
-            umma_commit(bar(B_SFULL + 0));
-            if (kMmaOrder == 1) {
-              ok = mbar_wait_spin(bar(sfree_bar(1)), g & 1u, SITE_MMA);
-              if (!ok) break;
-              tc_fence_after();
-            }
-            issue_qk(1, sk);
-            umma_commit(bar(B_SFULL + 1));
+            issue_qk(sk);
+            umma_commit(bar(B_SFULL + tq));
             umma_commit(bar(B_KVEMPTY + sk));
             if (j + 1 == n - 1) umma_commit(bar(B_QEMPTY));
           }
           ok = mbar_wait_spin(bar(B_KVFULL + sv), (iv / kStages) & 1u, SITE_MMA) &&
-               mbar_wait_spin(bar(pready_bar(0)), g & 1u, SITE_MMA);
+               mbar_wait_spin(bar(pready_bar(tq)), g & 1u, SITE_MMA);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(0, sv, j > 0 ? 1u : 0u);
-          umma_commit(bar(B_PVDONE + 0));
-          if (kMmaOrder == 1) {
-            ok = mbar_wait_spin(bar(pready_bar(1)), g & 1u, SITE_MMA);
-            if (!ok) break;
-            tc_fence_after();
-          }
-          issue_pv(1, sv, j > 0 ? 1u : 0u);
-          umma_commit(bar(B_PVDONE + 1));
+          issue_pv(sv, j > 0 ? 1u : 0u);
+          umma_commit(bar(B_PVDONE + tq));
           umma_commit(bar(B_KVEMPTY + sv));
         }
         L += 2 * n;
@@ -455,14 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         Kb += n;
         ++uc;
       }
-      umma_commit(bar(B_DRAIN));
-      mbar_wait_drain(bar(B_DRAIN), 0, SITE_DRAIN);
+      umma_commit(bar(B_DRAIN + tq));
+      mbar_wait_drain(bar(B_DRAIN + tq), 0, SITE_DRAIN);
     }
     __syncwarp();
   } else if (warp >= kWarpRope0) {
     // ------------------------------------------------------------ RoPE helpers (K tiles)
     regs_dec<kRegsHelper>();
-    const int tid = threadIdx.x - kWarpRope0 * 32;  // 0..63
+    const int tid = threadIdx.x - kWarpRope0 * 32;  // 0..31
     bool ok = true;
     uint32_t L = 0, Kb = 0;
     int uc = 0;
@@ -478,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok) {
             uint8_t* tile = smem + kOffKV + s * kTileBytes;
 #pragma unroll 1
-            for (int rr = tid; rr < kBN; rr += 64) {
+            for (int rr = tid; rr < kBN; rr += 32) {
               const int key = j * kBN + rr;
               if (key < p.S)
                 rope_row_smem(tile, kHalf, rr, p.cos + static_cast<size_t>(key) * kD,
