@@ -13,7 +13,8 @@
 // heads of the group (GQA by address, no KV duplication).
 //
 // Persistent CTAs (one per SM) walk the units heaviest-first (causal: most K tiles
-// first) in snake order over the rounds, so each SM gets a balanced share.  Nothing
+// first; in bands of 16 query blocks that keep the CTAs reading one K/V head together)
+// in snake order over the rounds, so each SM gets a balanced share.  Nothing
 // drains between units: the K/V ring and every barrier phase run on across them, the
 // next unit's Q is prefetched into L2 and loaded as soon as the last QK^T of the
 // current unit is done, the softmax threads rotate it before the current unit's
@@ -62,6 +63,7 @@ constexpr int kRowsPerHead = kBM / kG;        // 32
 constexpr int kPosPerCta = 2 * kRowsPerHead;  // 64
 constexpr int kBN = 128;                      // keys per K/V tile
 constexpr int kStages = 3;                    // K/V ring stages
+constexpr int kBand = 16;                     // query blocks per band of the unit order
 constexpr int kTileBytes = 128 * 128 * 2;     // Q, P, K and V tiles: 32 KB
 constexpr int kHalf = kTileBytes / 2;         // one 64-column swizzle block of 128 rows
 constexpr int kSoftmaxThreads = 512;  // warps 0-15
@@ -199,12 +201,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int u = i * n_ctas + c;
     return u < p.n_units ? u : -1;
   };
+  // Unit order: bands of kBand query blocks, heaviest band first; inside a band the blocks
+  // of one (sequence, kv head) are consecutive.  A round of 148 CTAs then streams the K/V
+  // of ~9 (sequence, kv head) pairs, each read by ~16 CTAs at nearly the same time, instead
+  // of 32 pairs read by ~4.6 CTAs each: more K/V tile loads hit in L2 (+2.8 % measured
+  // at seq 8192, batch 4, against one block per pair per band).
   auto decode = [&](int u) -> Unit {
     const int per_qb = p.B * p.kv_count;
-    const int qb = p.n_qblocks - 1 - u / per_qb;
-    const int rem = u % per_qb;
-    const int b = rem / p.kv_count;
-    const int kvh = p.kv_begin + rem % p.kv_count;
+    const int band_units = kBand * per_qb;
+    const int band = u / band_units;
+    const int nb = min(kBand, p.n_qblocks - band * kBand);  // the last band may be partial
+    const int rem = u - band * band_units;
+    const int pair = rem / nb;
+    const int qb = p.n_qblocks - 1 - (band * kBand + rem % nb);
+    const int b = pair / p.kv_count;
+    const int kvh = p.kv_begin + pair % p.kv_count;
     Unit x;
     x.p0 = qb * kPosPerCta;
     x.n_kv = causal ? min(n_kv_all, (x.p0 + kPosPerCta - 1) / kBN + 1) : n_kv_all;
