@@ -3,7 +3,8 @@
 // These reproduce each stage of the golden model with its bf16 boundary
 // rounding (llama3_attention_golden_model.py:124-190):
 //   rope_cache_kernel  build_rope_cache   :124-130
-//   rope_kernel        apply_rope          :133-139 (used :162-164)
+//   rope_kernel        apply_rope          :133-139 (used :162-164); rope128_kernel is its
+//                      16-byte vectorised form for head_dim 128
 //   scores_kernel      to_bf16(q k^T * s)  :175-176
 //   mask_kernel        to_bf16(s + triu)   :180-181
 //   word_mask_kernel   HLS attention_mask  attention_mask_module/src/attention_mask.cpp:3-58
@@ -62,6 +63,49 @@ __global__ void rope_kernel(const uint16_t* x, uint16_t* y, const uint16_t* cos,
     const float y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
     y[row * D + d] = f2bf_bits(y0);
     y[row * D + d + half] = f2bf_bits(y1);
+  }
+}
+
+// rope_kernel's arithmetic for two adjacent pairs packed in bf16x2 words: xa holds
+// x[d], x[d+1], xb holds x[d+64], x[d+65]; ca/sa the table words at d, cb/sb at d+64.
+__device__ __forceinline__ void rope_words(uint32_t xa, uint32_t xb, uint32_t ca, uint32_t cb, uint32_t sa,
+                                           uint32_t sb, uint32_t& ya, uint32_t& yb) {
+  uint32_t out_a = 0, out_b = 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int sh = 16 * k;
+    const float x0 = bf2f_bits(static_cast<uint16_t>(xa >> sh)), x1 = bf2f_bits(static_cast<uint16_t>(xb >> sh));
+    const float c0 = bf2f_bits(static_cast<uint16_t>(ca >> sh)), s0 = bf2f_bits(static_cast<uint16_t>(sa >> sh));
+    const float c1 = bf2f_bits(static_cast<uint16_t>(cb >> sh)), s1 = bf2f_bits(static_cast<uint16_t>(sb >> sh));
+    const float y0 = __fadd_rn(__fmul_rn(x0, c0), __fmul_rn(-x1, s0));
+    const float y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
+    out_a |= static_cast<uint32_t>(f2bf_bits(y0)) << sh;
+    out_b |= static_cast<uint32_t>(f2bf_bits(y1)) << sh;
+  }
+  ya = out_a;
+  yb = out_b;
+}
+
+// head_dim 128 with 16-byte aligned tensors: one thread per (row, 8 consecutive pairs),
+// 16-byte loads and stores, the same per-element arithmetic as rope_kernel (bit-identical).
+// This is the K pre-pass of the prefill step, so it runs at HBM speed instead of
+// element by element.
+__global__ void rope128_kernel(const uint4* x, uint4* y, const uint4* cos, const uint4* sin, int rows, int S,
+                               int pos0) {
+  const int n = rows * 8;  // 8 chunks of 8 pairs per row; each row is 16 uint4
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += gridDim.x * blockDim.x) {
+    const int row = idx >> 3, c = idx & 7;
+    const long long xo = static_cast<long long>(row) * 16 + c;
+    const long long to = static_cast<long long>(pos0 + row % S) * 16 + c;
+    const uint4 a = x[xo], b = x[xo + 8];
+    const uint4 ca = __ldg(cos + to), cb = __ldg(cos + to + 8), sa = __ldg(sin + to), sb = __ldg(sin + to + 8);
+    uint4 ya, yb;
+    rope_words(a.x, b.x, ca.x, cb.x, sa.x, sb.x, ya.x, yb.x);
+    rope_words(a.y, b.y, ca.y, cb.y, sa.y, sb.y, ya.y, yb.y);
+    rope_words(a.z, b.z, ca.z, cb.z, sa.z, sb.z, ya.z, yb.z);
+    rope_words(a.w, b.w, ca.w, cb.w, sa.w, sb.w, ya.w, yb.w);
+    y[xo] = ya;
+    y[xo + 8] = yb;
   }
 }
 
@@ -170,6 +214,15 @@ extern "C" int gqa_rope_bf16(const void* x, void* y, const void* cos, const void
   if (!x || !y || !cos || !sin || num_heads <= 0 || seq_len <= 0 || head_dim <= 0 || (head_dim & 1) || pos0 < 0)
     return GQA_ERR_INVALID_ARGUMENT;
   const long long n = static_cast<long long>(num_heads) * seq_len * (head_dim / 2);
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (head_dim == 128 && a16(x) && a16(y) && a16(cos) && a16(sin) &&
+      static_cast<long long>(num_heads) * seq_len * 8 <= (1LL << 30)) {
+    const int rows = num_heads * seq_len;
+    rope128_kernel<<<grid_for(static_cast<long long>(rows) * 8, 256), 256, 0, stream>>>(
+        static_cast<const uint4*>(x), static_cast<uint4*>(y), static_cast<const uint4*>(cos),
+        static_cast<const uint4*>(sin), rows, seq_len, pos0);
+    return launch_status();
+  }
   rope_kernel<<<grid_for(n, 256), 256, 0, stream>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y),
                                                     static_cast<const uint16_t*>(cos),
                                                     static_cast<const uint16_t*>(sin), num_heads, seq_len, head_dim,
