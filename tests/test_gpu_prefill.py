@@ -127,6 +127,42 @@ def test_edge_shapes_vs_oracle(B, S, causal, rope):
     _check_rows(out, qr, kr, bf16_words(v), [_all_rows(Hq, S)] * B, causal=causal, tag=f"S={S}")
 
 
+@pytest.mark.parametrize("kv_heads", [None, (1, 1)])
+def test_banded_unit_order_covers_every_block(kv_heads):
+    """Units run in bands of 16 query blocks per (sequence, kv head), heaviest band first.
+
+    S = 1100 gives 18 query blocks (one full band and a partial one) and batch 3 makes
+    several (sequence, kv head) pairs per band; with a kv-head subset the pairs per band
+    change again.  Every output row must be written once and match exact attention: the
+    output starts as NaN, and one row of every query block of every (sequence, head) is
+    checked against the oracle.
+    """
+    B, Hq, Hkv, S = 3, 8, 2, 1100
+    q = randn_bf16((B, Hq, S, 128), 41)
+    k = randn_bf16((B, Hkv, S, 128), 42)
+    v = randn_bf16((B, Hkv, S, 128), 43)
+    cos, sin = kernels.rope_cache(S)
+    out = torch.full((B, Hq, S, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+    kernels.prefill(q, k, v, cos, sin, rope_q=True, rope_k=True, kv_heads=kv_heads, out=out)
+    kernels.device_check()
+    h0, hn = (0, Hq) if kv_heads is None else (kv_heads[0] * 4, kv_heads[1] * 4)
+    assert torch.isfinite(out[:, h0:h0 + hn].float()).all()
+    if kv_heads is not None:
+        assert torch.isnan(out[:, :h0].float()).all() and torch.isnan(out[:, h0 + hn:].float()).all()
+    qr, kr = _rotated_words(q, S), _rotated_words(k, S)
+    rows = []
+    for b in range(B):
+        heads, pos = [], []
+        for h in range(h0, h0 + hn):
+            for qb in range((S + 63) // 64):
+                p = qb * 64 + (7 * h + 13 * b + 5 * qb) % 64
+                if p < S:
+                    heads.append(h)
+                    pos.append(p)
+        rows.append((np.array(heads), np.array(pos)))
+    _check_rows(out, qr, kr, bf16_words(v), rows, tag=f"banded kv_heads={kv_heads}")
+
+
 def test_fused_rope_equals_prerotated_inputs():
     B, Hq, Hkv, S = 2, 32, 8, 320
     q = randn_bf16((B, Hq, S, 128), 1)
