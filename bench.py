@@ -231,13 +231,24 @@ def run_short_prefills(args, hq, hkv, dev, stream, world) -> dict:
             sess.run_device()
         kernels.device_check(dev)
         n = 200
-        ms = time_loop(sess.run_device, n, world, stream) / n
+        ms_launch = time_loop(sess.run_device, n, world, stream) / n
         kernels.device_check(dev)
+        # the same step replayed from a CUDA graph: one host call instead of two Python launches
+        graph = sess.capture()
+        for _ in range(3):
+            graph.replay()
+        ms = time_loop(graph.replay, n, world, stream) / n
+        kernels.device_check(dev)
+        ref = sess.run_device().clone()
+        graph.replay()
+        same = bool(torch.equal(ref, sess.o))
         fl = causal_flops(1, HQ, S, D)  # every rank runs its heads of the one sequence
         out[key] = {"seq_len": S, "batch": 1, "ms_per_step": ms, "value": fl / (ms * 1e-3) / 1e12,
                     "unit": "TFLOP/s", "steps": n, "launches_per_step": sess.launches_per_step(),
+                    "launch": "CUDA graph replay (PrefillSession.capture)", "graph_equals_direct": same,
+                    "ms_per_step_direct_launches": ms_launch,
                     "l2": "inputs fit in L2 (no flush between steps)"}
-        del sess
+        del graph, sess
     return out
 
 

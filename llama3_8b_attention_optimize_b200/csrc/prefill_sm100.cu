@@ -13,8 +13,9 @@
 // heads of the group (GQA by address, no KV duplication).
 //
 // Persistent CTAs (one per SM) walk the units heaviest-first (causal: most K tiles
-// first; in bands of 16 query blocks that keep the CTAs reading one K/V head together)
-// in snake order over the rounds, so each SM gets a balanced share.  Nothing
+// first; in bands of 16 query blocks that keep the CTAs reading one K/V head together
+// when many (sequence, kv head) pairs share a round) in snake order over the rounds, so
+// each SM gets a balanced share.  Nothing
 // drains between units: the K/V ring and every barrier phase run on across them, the
 // next unit's Q is prefetched into L2 and loaded as soon as the last QK^T of the
 // current unit is done, the softmax threads rotate it before the current unit's
@@ -63,7 +64,7 @@ constexpr int kRowsPerHead = kBM / kG;        // 32
 constexpr int kPosPerCta = 2 * kRowsPerHead;  // 64
 constexpr int kBN = 128;                      // keys per K/V tile
 constexpr int kStages = 3;                    // K/V ring stages
-constexpr int kBand = 16;                     // query blocks per band of the unit order
+constexpr int kBand = 16;                     // query blocks per band of the unit order (when banded)
 constexpr int kTileBytes = 128 * 128 * 2;     // Q, P, K and V tiles: 32 KB
 constexpr int kHalf = kTileBytes / 2;         // one 64-column swizzle block of 128 rows
 constexpr int kSoftmaxThreads = 512;  // warps 0-15
@@ -128,6 +129,7 @@ enum : int {  // error sites reported through g_gqa_dev_error
 
 struct Params {
   int B, S, Hq, Hkv, kv_begin, kv_count, n_qblocks, n_units;
+  int band;  // query blocks per band of the unit order: kBand or 1 (see launch_prefill)
   int flags;
   float scale_log2;
   const uint16_t* cos;  // [>= S][128] bf16 (cat(freqs, freqs) layout)
@@ -201,19 +203,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int u = i * n_ctas + c;
     return u < p.n_units ? u : -1;
   };
-  // Unit order: bands of kBand query blocks, heaviest band first; inside a band the blocks
-  // of one (sequence, kv head) are consecutive.  A round of 148 CTAs then streams the K/V
-  // of ~9 (sequence, kv head) pairs, each read by ~16 CTAs at nearly the same time, instead
-  // of 32 pairs read by ~4.6 CTAs each: more K/V tile loads hit in L2 (+2.8 % measured
-  // at seq 8192, batch 4, against one block per pair per band).
+  // Unit order: bands of p.band query blocks, heaviest band first; inside a band the blocks
+  // of one (sequence, kv head) are consecutive.  With 32 (sequence, kv head) pairs a round
+  // of 148 CTAs then streams the K/V of ~9 pairs, each read by ~16 CTAs at nearly the same
+  // time, instead of 32 pairs read by ~4.6 CTAs each: more K/V tile loads hit in L2 (+2.8 %
+  // measured at seq 8192, batch 4).  p.band = 1 is plain heaviest-first order.
   auto decode = [&](int u) -> Unit {
     const int per_qb = p.B * p.kv_count;
-    const int band_units = kBand * per_qb;
+    const int band_units = p.band * per_qb;
     const int band = u / band_units;
-    const int nb = min(kBand, p.n_qblocks - band * kBand);  // the last band may be partial
+    const int nb = min(p.band, p.n_qblocks - band * p.band);  // the last band may be partial
     const int rem = u - band * band_units;
     const int pair = rem / nb;
-    const int qb = p.n_qblocks - 1 - (band * kBand + rem % nb);
+    const int qb = p.n_qblocks - 1 - (band * p.band + rem % nb);
     const int b = pair / p.kv_count;
     const int kvh = p.kv_begin + pair % p.kv_count;
     Unit x;
@@ -701,6 +703,14 @@ int launch_prefill(const void* q, const void* k, const void* v, void* o, const v
   p.cos = static_cast<const uint16_t*>(cos);
   p.sin = static_cast<const uint16_t*>(sin);
   const int grid = static_cast<int>(n_units < sms ? n_units : sms);
+  // Bands only pay when the (sequence, kv head) pairs outnumber what a round shares by
+  // itself (grid / pairs query blocks of each pair per round, fewer than kBand), and when
+  // there are enough rounds that bands of unequal units still balance across the SMs.
+  // Batch 1 with 8 kv heads (each K/V stream already read by ~18 CTAs per round) or a
+  // problem of a few rounds keeps the plain heaviest-first order: at seq 2048 the bands
+  // would leave the busiest SM with 1.43x the mean work instead of 1.09x.
+  const long long pairs = static_cast<long long>(B) * kv_count;
+  p.band = (pairs * kBand > grid && n_units >= 8LL * grid) ? kBand : 1;
   prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }

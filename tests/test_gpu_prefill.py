@@ -127,17 +127,18 @@ def test_edge_shapes_vs_oracle(B, S, causal, rope):
     _check_rows(out, qr, kr, bf16_words(v), [_all_rows(Hq, S)] * B, causal=causal, tag=f"S={S}")
 
 
-@pytest.mark.parametrize("kv_heads", [None, (1, 1)])
-def test_banded_unit_order_covers_every_block(kv_heads):
-    """Units run in bands of 16 query blocks per (sequence, kv head), heaviest band first.
+@pytest.mark.parametrize("B,Hkv,S,kv_heads", [(2, 8, 4800, None), (3, 2, 1100, None), (3, 2, 1100, (1, 1))])
+def test_banded_unit_order_covers_every_block(B, Hkv, S, kv_heads):
+    """Unit order: bands of 16 query blocks per (sequence, kv head) when the pairs are many
+    and the problem has enough rounds, else plain heaviest-first order.
 
-    S = 1100 gives 18 query blocks (one full band and a partial one) and batch 3 makes
-    several (sequence, kv head) pairs per band; with a kv-head subset the pairs per band
-    change again.  Every output row must be written once and match exact attention: the
-    output starts as NaN, and one row of every query block of every (sequence, head) is
-    checked against the oracle.
+    Batch 2 x 8 kv heads at S = 4800 (75 query blocks: 4 full bands and a partial one,
+    16 pairs, 1200 units) takes the banded order; batch 3 x 2 kv heads at S = 1100, with
+    all or a subset of the kv heads, takes the plain one.  Every output row must be
+    written once and match exact attention: the output starts as NaN, and one row of
+    every query block of every (sequence, head) is checked against the oracle.
     """
-    B, Hq, Hkv, S = 3, 8, 2, 1100
+    Hq = 4 * Hkv
     q = randn_bf16((B, Hq, S, 128), 41)
     k = randn_bf16((B, Hkv, S, 128), 42)
     v = randn_bf16((B, Hkv, S, 128), 43)
@@ -278,3 +279,26 @@ def test_prefill_stream_overlapped_host_steps_match_device_results():
     kernels.device_check()
     for (_, _, _, out), ref in zip(steps, refs):
         assert torch.equal(out, ref)
+
+
+def test_prefill_session_graph_replay_equals_direct_launches():
+    """PrefillSession.capture(): replaying the recorded step (K pre-pass + fused kernel)
+    gives the direct launches' output bit for bit, also after new inputs are copied into
+    the session's buffers in place."""
+    from llama3_8b_attention_optimize_b200.session import PrefillSession
+    sess = PrefillSession(1, 2048, 32, 8)
+    sess.q.copy_(randn_bf16(sess.shape_q, 61))
+    sess.k.copy_(randn_bf16(sess.shape_kv, 62))
+    sess.v.copy_(randn_bf16(sess.shape_kv, 63))
+    graph = sess.capture()
+    for seed in (0, 10):
+        sess.q.copy_(randn_bf16(sess.shape_q, 71 + seed))
+        sess.k.copy_(randn_bf16(sess.shape_kv, 72 + seed))
+        sess.v.copy_(randn_bf16(sess.shape_kv, 73 + seed))
+        direct = sess.run_device().clone()
+        sess.o.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        kernels.device_check()
+        assert torch.equal(sess.o, direct)
+    del graph
